@@ -1,0 +1,320 @@
+#!/usr/bin/env python
+"""MoE expert-layer benchmark on B200: the Qwen3.6-35B-A3B-shaped decode configuration (40 stacked layers, every expert
+resident in HBM, IQ3_XXS routed experts + Q8_0 shared expert, T tokens per step).
+
+One step = one decode step through all 40 MoE layers for T tokens (router GEMV + top-8 + grouping + grouped expert
+GEMVs + shared expert + gated combine + the next layer's RMS/q8_1), replayed as one CUDA graph.  The metric is
+MoE-layer tokens/s (T / mean layer time) with microseconds per layer beside it.  Decode does not shard: with --gpus N
+each rank runs its own replica (weak scaling) and `value` sums the replicas.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl tsb|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_LAYERS = 40
+METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region: median SM clock, max clock, throttle reasons seen."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 3 + i and r[3 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def reference_arm(args):
+    """The reference's own CPU expert path (oracle/_ref) on this host's cores, same metric and config."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    from tinystrata_b200 import synth
+    cfg = synth.QWEN
+    vals = []
+    per = max(3.0, 60.0 / max(1, args.steps + args.warmup))
+    for i in range(args.warmup + args.steps):
+        r = O.cpu_baseline_decode(cfg, seconds=per, seed=1 + i)
+        if i >= args.warmup:
+            vals.append(r)
+    v = float(np.mean([r["value"] for r in vals]))
+    line = {"metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": N_LAYERS * args.tokens / v * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dp (q8_1/Q8_K x IQ3_XXS)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"decode T={args.tokens}, 1 layer x 256 IQ3_XXS experts in host memory "
+                                   f"(routed experts; the reference runs the shared expert on the GPU)",
+                       "model": "qwen3.6-35b-a3b-shaped MoE layer", "tokens": args.tokens},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": vals[0]["cores"], "kind": "reference",
+                             "sample": vals[0]["sample"]},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def build_stack(cfg, T, device, seed=1):
+    import torch
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+    st = synth.device_layers(cfg, N_LAYERS, seed, device)
+    H, E, K = cfg["n_embd"], cfg["n_expert"], cfg["n_used"]
+    # routing made disjoint across the step's tokens: token t's experts are {8t .. 8t+7} (mod 256), planted in every
+    # layer's router on input dimension d_t, and the inputs carry a spike there large enough to survive 40 layers
+    dims = [(7 + 61 * t) % H for t in range(T)]
+    for l in range(N_LAYERS):
+        for t in range(T):
+            for k in range(K):
+                st["routers"][l, (t * K + k) % E, dims[t]] = 1.0 + 0.01 * k
+    layers = [TS.MoELayer(cfg, st["blobs"][l], st["routers"][l], st["sh_blobs"][l], max_tokens=max(T, 1))
+              for l in range(N_LAYERS)]
+    rng = np.random.default_rng(seed)
+    x0 = rng.normal(0, 1, size=(T, H)).astype(np.float32)
+    for t in range(T):
+        x0[t, dims[t]] = 1e8
+    return st, layers, x0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--impl", default="tsb", choices=["tsb", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    cfg = synth.QWEN
+    T, H, K, E = args.tokens, cfg["n_embd"], cfg["n_used"], cfg["n_expert"]
+    st, layers, x0 = build_stack(cfg, T, device)
+    torch.cuda.synchronize()
+    x = torch.empty((T, H), device=device)
+    h = torch.empty((T, H), device=device)
+    hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
+    x0_dev = torch.from_numpy(x0).to(device)
+    x0_host = torch.from_numpy(x0).pin_memory()
+    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+
+    stream = torch.cuda.Stream(device)
+
+    def step_body():
+        TS.rms_norm_q8_1(x, h, hq, stream=stream)
+        for M in layers:
+            M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream)
+
+    # verification pass (eager, untimed): routing actually taken, and finite outputs
+    with torch.cuda.stream(stream):
+        x.copy_(x0_dev)
+        step_body()
+    stream.synchronize()
+    assert TS.device_error() == 0
+    assert torch.isfinite(x).all(), "non-finite layer output"
+    distinct = [int(torch.unique(M.ids[:T]).numel()) for M in layers]
+    L, Ls = layers[0].L, layers[0].Ls
+    bytes_layer = [d * L.bytes + Ls.bytes + (E + 1) * H * 4 for d in distinct]
+    alg_bytes_per_layer = float(np.mean(bytes_layer))
+
+    # capture one step as a graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        x.copy_(x0_dev)
+        with torch.cuda.graph(graph, stream=stream):
+            step_body()
+    launches_per_step = 1 + N_LAYERS * 8   # rms; per layer: logits, top-k, group, gu, down, shared gu, shared down, combine
+
+    def replay(n):
+        for _ in range(n):
+            graph.replay()
+
+    # device-timed region (inputs resident)
+    with torch.cuda.stream(stream):
+        x.copy_(x0_dev)
+        replay(max(3, args.warmup))
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                x.copy_(x0_dev)
+                graph.replay()
+            ev1.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if ws > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_layer = ms * 1e3 / N_LAYERS
+    value = ws * T / (us_layer * 1e-6)
+
+    # end to end: host input -> device, the 40 layers, device -> host, every step
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            x.copy_(x0_host, non_blocking=True)
+            graph.replay()
+            out_host.copy_(x, non_blocking=True)
+        e1.record(stream)
+    stream.synchronize()
+    barrier()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if ws > 1:
+        t = torch.tensor([ms_e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_value = ws * T / (ms_e2e * 1e3 / N_LAYERS * 1e-6)
+
+    # the dominant kernel alone: the routed gate/up GEMV of each layer, CUDA events on its stream (cold: 40 layers
+    # of distinct weights between launches of the same layer)
+    TS.native_expert_set_phase(1)
+    gu_ms = []
+    with torch.cuda.stream(stream):
+        for rep in range(3):
+            for M in layers:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                TS.native_expert_grouped(M.L, M.groups, T * K, T * K, hq, M.scratch, M.parts, stream=stream)
+                b.record(stream)
+                gu_ms.append((a, b))
+    stream.synchronize()
+    TS.native_expert_set_phase(0)
+    gu_avg_ms = float(np.mean([a.elapsed_time(b) for a, b in gu_ms[len(layers):]]))
+    gu_bytes = float(np.mean([d * L.up_off * 2 for d in distinct]))
+    peak, peak_kind = peaks()
+    gu_gbs = gu_bytes / (gu_avg_ms * 1e-3) / 1e9
+    layer_gbs = alg_bytes_per_layer / (us_layer * 1e-6) / 1e9
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        try:
+            from oracle import oracle as O
+            cpu = O.cpu_baseline_decode(cfg, seconds=10.0)
+        except Exception as e:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 dp4a (q8_1 x IQ3_XXS / Q8_0), fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"decode T={T} through 40 resident Qwen3.6-35B-A3B-shaped MoE layers",
+                       "model": "qwen3.6-35b-a3b-shaped MoE layer x40", "tokens_per_step": T, "layers": N_LAYERS,
+                       "hidden": H, "experts": E, "top_k": K, "n_ff": cfg["n_ff"], "routed": "IQ3_XXS",
+                       "shared": "Q8_0", "parallelism": f"replicas x{ws}",
+                       "distinct_experts_per_layer": float(np.mean(distinct)),
+                       "l2": "inputs larger than L2 (12.3 GB of expert weights, 40 distinct layers per step)"},
+            "us_per_layer": us_layer,
+            "layer_hbm_gbs": layer_gbs,
+            "roofline": {"bound": "hbm", "kernel": "k_expert_gu (routed gate/up + SwiGLU)", "achieved": gu_gbs,
+                         "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak, "peak_kind": peak_kind,
+                         "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
+                         "avg_launch_ms": gu_avg_ms,
+                         "layer_frac": layer_gbs / peak, "layer_algorithmic_bytes": alg_bytes_per_layer},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if ws > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,137 @@
+/*
+ * tsb_moe.h - C ABI of the B200 MoE expert-layer path (libtsb_moe.so).
+ *
+ * Drop-in boundary for TinyStrata's expert-layer entry points.  Each function names the reference interface it
+ * replaces (paths inside the TinyStrata tree).  Conventions, as the reference's:
+ *   - every pointer argument is a DEVICE pointer unless stated; buffers are caller-owned, calls allocate nothing on the
+ *     stream path and never synchronise it (counts such as n_groups stay on the device, so calls are graph-capturable);
+ *   - ggml type ids: Q4_0 = 2, Q8_0 = 8, Q4_K = 12, Q6_K = 14, IQ3_XXS = 18, IQ3_S = 21; weights are raw GGUF blocks;
+ *   - activations are q8_1 blocks (fp16 d, fp16 sum, 32 int8 codes: 36 bytes per 32 values);
+ *   - `stream` is a cudaStream_t (0 = the legacy default stream).
+ * Every call returns TSB_OK (0) or a negative tsb_status; tsb_last_error() describes the last failure of the calling
+ * thread.  Nothing here exits or throws.
+ */
+#ifndef TSB_MOE_H
+#define TSB_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TSB_MOE_ABI_VERSION 1
+
+enum tsb_status {
+    TSB_OK = 0,
+    TSB_ERR_ARG = -1,          /* a null pointer, a bad size or count */
+    TSB_ERR_UNSUPPORTED = -2,  /* a format or shape without a kernel */
+    TSB_ERR_CUDA = -3,         /* a CUDA launch or runtime error (see tsb_last_error) */
+    TSB_ERR_ALIGN = -4,        /* a buffer or blob offset not aligned as the kernel needs */
+    TSB_ERR_WORKSPACE = -5     /* caller workspace smaller than the query said */
+};
+
+/* The layout of one expert blob: [gate rows | up rows | down rows] of raw GGUF blocks.
+ * Replaces strata::kernels::NativeExpertLayout (include/strata/kernels/iq_kernels.hpp:45-53). */
+typedef struct tsb_expert_layout {
+    int32_t gu_type, d_type;
+    int64_t n_embd, n_ff;
+    uint64_t gu_row, d_row;      /* bytes per row */
+    uint64_t up_off, down_off;   /* byte offsets inside the blob */
+    uint64_t bytes;              /* the whole blob */
+} tsb_expert_layout;
+
+int tsb_moe_abi_version(void);
+/* The calling thread's last error message ("" when none). */
+const char* tsb_last_error(void);
+/* The current device's error word: non-zero when a kernel's bounded wait gave up (the kernel then returned early).
+ * `clear` resets it.  Reads device memory (synchronous). */
+int tsb_device_error(unsigned* code, int clear);
+
+/* --------------------------------------------------------------------------------------------- formats */
+/* Replaces iq_supported / iq_row_bytes (iq_kernels.hpp:17-21). */
+int tsb_type_supported(int ggml_type);
+int64_t tsb_row_bytes(int ggml_type, int64_t n);
+/* Replaces native_expert_layout / native_expert_supported / native_expert_scratch_bytes (iq_kernels.hpp:53-62). */
+int tsb_native_expert_layout(int gu_type, int d_type, int64_t n_embd, int64_t n_ff, tsb_expert_layout* out);
+int tsb_native_expert_supported(int gu_type, int d_type, int64_t n_embd, int64_t n_ff);
+uint64_t tsb_native_expert_scratch_bytes(int64_t cap_entries, int64_t n_ff);
+
+/* --------------------------------------------------------------------------------------------- activations */
+/* q8_1 blocks of n_rows rows of n_cols floats (n_cols % 32 == 0).  Replaces quantize_q8_1_rows (iq_kernels.hpp:24)
+ * and native_quantize_q8_1 (native_mmvq.hpp:38): the same blocks bit for bit. */
+int tsb_quantize_q8_1_rows(const float* x, int64_t n_rows, int64_t n_cols, void* y, void* stream);
+
+/* --------------------------------------------------------------------------------------------- router */
+/* fp32 router logits: logits[t * ld + o] = W[o] . h[t] for o < n_out (W row-major [n_out][n_in], 16-byte aligned).
+ * Replaces the f32mm router GEMV (src/qwen35/q36_engine.cu:2106-2131; the shared-expert gate is row n_expert). */
+int tsb_router_logits_f32(const float* W, const float* h, float* logits, int n_in, int n_out, int n_tok, int ld,
+                          void* stream);
+/* Softmax top-k with renormalised weights, ids and weights [n_tok][k], logits row stride ld.
+ * Replaces native_router_topk (include/strata/kernels/native_router.hpp:5-6), generalised from (256, 8) to any
+ * multiple of 32 experts up to 512 and k <= 32; the (256, 8) case gives the same ids and weights bit for bit. */
+int tsb_native_router_topk(const float* logits, int32_t* ids, float* weights, int n_expert, int k, int n_tok, int ld,
+                           void* stream);
+/* Gemma 4 / LFM2 routing: gate 0 = softmax(logit * in_scale), 1 = sigmoid; the n_used largest of p + bias; weights
+ * the bare p, divided by max(sum, 6.103515625e-5) when norm, times escale[id] when given, times w_scale when non-zero.
+ * Replaces route_rows (include/strata/gemma4/kernels.hpp; src/gemma4/kernels.cu:289-356). */
+int tsb_route_rows(const float* logits, int n_expert, int n_used, int rows, int gate, float in_scale, const float* bias,
+                   const float* escale, int norm, float w_scale, int32_t* ids, float* w, void* stream);
+
+/* --------------------------------------------------------------------------------------------- dispatch */
+/* Decode grouping: one group per expert used (ascending id) with blob address blobs + id * blob_stride, its entries
+ * (entry e = t * K + k) in entry order: grp_ptr[<= n_ent], grp_start[<= n_ent + 1], *n_groups, ent_dst[e'] = e,
+ * ent_tok[e'] = e / K.  Replaces k_group / k_group_small (src/qwen35/q36_engine.cu:396-422,
+ * src/qwen35/q36_kernels.cuh:347-381). */
+int tsb_moe_group(const int32_t* ids, int n_ent, int K, int n_expert, const void* blobs, uint64_t blob_stride,
+                  uint64_t* grp_ptr, int32_t* grp_start, int32_t* n_groups, int32_t* ent_dst, int32_t* ent_tok,
+                  void* stream);
+
+/* --------------------------------------------------------------------------------------------- experts */
+/* Grouped experts, SwiGLU: for each group g (blob grp_ptr[g]) and entry e in [grp_start[g], grp_start[g+1]):
+ * out[ent_dst[e]] = down(q8_1(silu(gate . x) * (up . x))) with x = token ent_tok[e] of x_q8_1 (n_embd / 32 blocks per
+ * token).  Counts are read on the device.  scratch: tsb_native_expert_scratch_bytes(cap_entries, n_ff) bytes.
+ * Replaces native_expert_grouped (include/strata/kernels/iq_kernels.hpp:75-78); grid_groups is accepted and, as
+ * there, never changes the results. */
+int tsb_native_expert_grouped(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                              const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                              int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, void* scratch, float* out,
+                              void* stream, int64_t grid_groups);
+/* The same with the activation chosen: act 0 SwiGLU, 1 GELU-tanh (Gemma 4), 2 SwiGLU with the inputs clamped to
+ * `limit` (LFM2).  Replaces gemma_native_mmvq_ids + geglu_rows / swiglu_clamp_rows + gemma_native_quantize_q8_1 +
+ * the down gemma_native_mmvq_ids (src/gemma4/matvec.hpp:150-171, include/strata/gemma4/kernels.hpp). */
+int tsb_native_expert_grouped_act(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                                  const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                                  int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, void* scratch,
+                                  float* out, int act, float limit, void* stream);
+
+/* Bench only: 0 = both expert kernels (default), 1 = gate/up + activation only, 2 = down only (reads the scratch the
+ * previous call left).  Replaces native_expert_set_mode's phase argument (iq_kernels.hpp:85).  Process-wide; set
+ * outside graph capture. */
+int tsb_native_expert_set_phase(int phase);
+
+/* --------------------------------------------------------------------------------------------- combine */
+/* x[t] += sum_k wts[t,k] parts[prow ? prow[t*K+k] : t*K+k] (fma in pick order) + sigmoid(sgate[t*sg_stride]) *
+ * shared[t] (shared / sgate may be null); with wn or h: h = x * rsqrt(mean(x^2) + eps) * wn (wn null = 1) and, with hq,
+ * hq = q8_1(h).  Replaces k_moe_out / k_moe_out_small (src/qwen35/q36_engine.cu:307-332,
+ * src/qwen35/q36_kernels.cuh:252-290). */
+int tsb_moe_combine(float* x, const float* parts, const int32_t* prow, const float* wts, int K, const float* shared,
+                    const float* sgate, int sg_stride, const float* wn, float* h, void* hq, int n, float eps, int n_tok,
+                    void* stream);
+/* h = x * rsqrt(mean(x^2) + eps) * wn (wn null = 1) and hq = q8_1(h) for n_tok rows (either output may be null).
+ * Replaces k_add_rms_q without the add (src/qwen35/q36_kernels.cuh:222-250): the layer input's norm and q8_1 image. */
+int tsb_rms_norm_q8_1(const float* x, const float* wn, float* h, void* hq, int n, float eps, int n_tok, void* stream);
+/* acc[t] += sum_k w[t,k] x[t*K+k], n values per row.  Replaces moe_sum (src/gemma4/kernels.cu:358-366). */
+int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, int rows, void* stream);
+
+/* --------------------------------------------------------------------------------------------- test hook */
+/* The per-call integer sums and float values of one weight row (n values) against one q8_1 activation, as the
+ * expert kernels compute them (calls in row_dot order, src/kernels/cuda/iq_kernels.cu:695-705).  Parity tests only. */
+int tsb_debug_row_calls(int ggml_type, const void* row, const void* x_q8_1, int64_t n, int32_t* sumi, float* val,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TSB_MOE_H */

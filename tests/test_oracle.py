@@ -1,0 +1,218 @@
+"""The oracle (oracle/tsb_oracle.c) against the reference's own compiled CPU kernels (golden fixtures made by
+tests/golden/make_golden.py, and oracle/_ref live when built), against ggml's gguf-py decoders, and the
+host-side routing / grouping / dispatch logic.  CPU only."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tinystrata_b200 import synth
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "ref_cpu_rows.npz")
+Q8K_BYTES = 292
+
+
+def q8k_values(xk: np.ndarray, n: int) -> np.ndarray:
+    """block_q8_K (float d, 256 int8, 16 int16 bsums) -> the values d * q."""
+    nb = n // 256
+    b = xk.reshape(-1, nb, Q8K_BYTES)
+    d = b[..., 0:4].copy().view(np.float32)[..., 0]
+    q = b[..., 4:260].view(np.int8).astype(np.float64)
+    return (d[..., None].astype(np.float64) * q).reshape(-1, n)
+
+
+def deq_rows(t, W, rows, n):
+    rb = O.row_bytes(t, n)
+    return np.stack([O.dequant_row(t, W[r * rb:(r + 1) * rb], n) for r in range(rows)]).astype(np.float64)
+
+
+@pytest.mark.parametrize("t", [synth.T_IQ3_XXS, synth.T_IQ3_S, synth.T_Q4_K])
+def test_decode_pinned_to_reference_cpu_rows(t):
+    """Row products of the reference's iq512_rows / kq256_rows (Q8_K activations) equal the oracle's decoded weights
+    times the same Q8_K values: pins the grids, sign tables, sub-block scales and block layouts."""
+    z = np.load(GOLDEN)
+    W, xk, y = z[f"t{t}_W"], z[f"t{t}_xq8k"], z[f"t{t}_y"]
+    n = z[f"t{t}_x"].shape[1]
+    rows = y.shape[1]
+    Wd = deq_rows(t, W, rows, n)
+    xd = q8k_values(xk, n)
+    mine = xd @ Wd.T
+    scale = np.abs(xd) @ np.abs(Wd).T
+    assert np.all(np.abs(mine - y) <= 2e-6 * scale + 1e-30), np.max(np.abs(mine - y) / scale)
+
+
+@pytest.mark.parametrize("t", [synth.T_IQ3_XXS, synth.T_IQ3_S, synth.T_Q4_K])
+def test_swiglu_pinned_to_reference_cpu_gu_rows(t):
+    z = np.load(GOLDEN)
+    blob, xk, ff = z[f"t{t}_blob"], z[f"t{t}_xq8k"], z[f"t{t}_ff"]
+    n = z[f"t{t}_x"].shape[1]
+    n_ff = ff.shape[1]
+    Wd = deq_rows(t, blob, 2 * n_ff, n)
+    xd = q8k_values(xk, n)
+    g, u = xd @ Wd[:n_ff].T, xd @ Wd[n_ff:].T
+    mine = g / (1.0 + np.exp(-g)) * u
+    assert np.allclose(mine, ff, rtol=2e-4, atol=1e-3 * np.abs(ff).max())
+
+
+def test_reference_cpu_live_matches_golden():
+    """When oracle/_ref is built here, re-run it: the fixtures are what the reference computes."""
+    R = O.ref_cpu()
+    if R is None:
+        pytest.skip("oracle/_ref not built (no reference tree)")
+    import subprocess, sys, tempfile, shutil
+    z = np.load(GOLDEN)
+    from tests.golden import make_golden as G
+    for t in (synth.T_IQ3_XXS, synth.T_IQ3_S, synth.T_Q4_K):
+        x = z[f"t{t}_x"]
+        xk = G.q8k(R, x)
+        assert np.array_equal(xk, z[f"t{t}_xq8k"])
+        y = G.ref_rows(R, t, z[f"t{t}_W"], x.shape[1], xk, z[f"t{t}_y"].shape[1])
+        assert np.array_equal(y, z[f"t{t}_y"])
+
+
+GGUF_NAMES = {synth.T_Q4_0: "Q4_0", synth.T_Q8_0: "Q8_0", synth.T_Q4_K: "Q4_K", synth.T_Q6_K: "Q6_K",
+              synth.T_IQ3_XXS: "IQ3_XXS", synth.T_IQ3_S: "IQ3_S"}
+
+
+@pytest.mark.parametrize("t", sorted(GGUF_NAMES))
+def test_dequant_matches_gguf_py(t):
+    """ggml's own Python decoders (the gguf package) agree with the oracle's for every format."""
+    gq = pytest.importorskip("gguf.quants")
+    rng = np.random.default_rng(t)
+    n = 512
+    W = synth.gen_matrix(rng, t, 4, n, 0.02)
+    cls = getattr(gq, GGUF_NAMES[t])
+    if hasattr(cls, "init_grid"):
+        cls.init_grid()
+    ref = gq.dequantize(W.reshape(4, -1), getattr(gq.GGMLQuantizationType, GGUF_NAMES[t]))
+    mine = deq_rows(t, W, 4, n)
+    assert np.allclose(mine, ref.reshape(4, n), rtol=1e-6, atol=1e-7)
+
+
+# ------------------------------------------------------------------------------------------------ q8_1 and calls
+def test_q8_1_quantizer_properties():
+    rng = np.random.default_rng(1)
+    x = rng.normal(0, 3, size=(7, 256)).astype(np.float32)
+    x[0, :32] = 0.0
+    q = O.quantize_q8_1(x)
+    d, s, codes = O.q8_1_unpack(q)
+    assert q.shape == (7, 8 * 36)
+    assert np.all(codes[0, 0] == 0) and d[0, 0] == 0
+    blocks = x.reshape(7, 8, 32)
+    amax = np.abs(blocks).max(-1)
+    assert np.allclose(d, (amax / 127).astype(np.float16).astype(np.float32))
+    assert np.all(np.abs(codes.astype(np.int32)) <= 127)
+    dd = (amax / 127)[..., None]
+    err = np.abs(codes * dd - blocks)
+    assert np.all(err <= dd * 0.5 + 1e-6)
+    assert np.allclose(s, blocks.sum(-1).astype(np.float16).astype(np.float32), rtol=2e-3, atol=1e-2)
+
+
+@pytest.mark.parametrize("t", sorted(GGUF_NAMES))
+def test_call_values_sum_to_the_decoded_dot(t):
+    """The per-call values (the reference's expressions) add up to the decoded weights times the q8_1 values, within
+    the integer truncation IQ3_XXS's scale step allows."""
+    rng = np.random.default_rng(100 + t)
+    n = 512
+    W = synth.gen_matrix(rng, t, 1, n, 0.02)
+    x = rng.normal(0, 1, size=(1, n)).astype(np.float32)
+    xq = O.quantize_q8_1(x)[0]
+    sumi, val = O.row_dot_calls(t, W, xq, n)
+    d, _, codes = O.q8_1_unpack(xq)
+    xv = (d[:, None] * codes).reshape(-1).astype(np.float64)
+    exact = float(O.dequant_row(t, W, n).astype(np.float64) @ xv)
+    got = float(val.astype(np.float64).sum())
+    tol = 1e-5 * float(np.abs(O.dequant_row(t, W, n)) @ np.abs(xv)) + 1e-6
+    if t == synth.T_IQ3_XXS:   # (ls*s + s/2)/2 truncates: at most one unit of d_w*d_x per call
+        tol += len(val) * float(np.abs(O.half_to_float(int(W[:2].view(np.uint16)[0]))) * d.max())
+    assert abs(got - exact) <= tol, (got, exact, tol)
+
+
+# ------------------------------------------------------------------------------------------------ routing
+def test_router_softmax_topk_matches_sorting():
+    rng = np.random.default_rng(7)
+    logits = rng.normal(0, 2, size=(64, 256)).astype(np.float32)
+    ids, w, near = O.router_softmax_topk(logits, 8)
+    assert near == 0
+    ref = np.argsort(-logits, axis=1, kind="stable")[:, :8]
+    assert np.array_equal(ids, ref)
+    p = np.exp(logits.astype(np.float64) - logits.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    sel = np.take_along_axis(p, ref, 1)
+    assert np.allclose(w, sel / sel.sum(1, keepdims=True), rtol=1e-5)
+
+
+def test_router_ties_pick_lowest_id():
+    logits = np.zeros((2, 256), np.float32)
+    logits[1, [5, 9, 200]] = 1.0
+    ids, w, _ = O.router_softmax_topk(logits, 8)
+    assert list(ids[0]) == list(range(8))
+    assert list(ids[1][:3]) == [5, 9, 200] and list(ids[1][3:]) == [0, 1, 2, 3, 4]
+    assert np.allclose(w[0], 1 / 8)
+
+
+def test_route_rows_modes():
+    rng = np.random.default_rng(3)
+    lg = rng.normal(0, 2, size=(16, 64)).astype(np.float32)
+    bias = rng.normal(0, 0.1, size=64).astype(np.float32)
+    ids, w = O.route_rows(lg, 4, 1, 1.0, bias, None, True, 0.0)
+    p = 1 / (1 + np.exp(-lg.astype(np.float64)))
+    ref = np.argsort(-(p + bias), axis=1, kind="stable")[:, :4]
+    assert np.array_equal(ids, ref)
+    sel = np.take_along_axis(p, ref, 1)
+    assert np.allclose(w, sel / sel.sum(1, keepdims=True), rtol=1e-5)
+    esc = rng.uniform(0.5, 2, size=64).astype(np.float32)
+    ids2, w2 = O.route_rows(lg, 8, 0, 0.5, None, esc, True, 0.0)
+    q = np.exp(lg * 0.5 - (lg * 0.5).max(1, keepdims=True))
+    ref2 = np.argsort(-q, axis=1, kind="stable")[:, :8]
+    assert np.array_equal(ids2, ref2)
+    s2 = np.take_along_axis(q / q.sum(1, keepdims=True), ref2, 1)
+    assert np.allclose(w2, s2 / s2.sum(1, keepdims=True) * esc[ref2], rtol=1e-5)
+
+
+def test_group_and_dispatch():
+    rng = np.random.default_rng(11)
+    T, K, E = 37, 8, 64
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    ge, gs, dst, tok = O.group(ids, E)
+    flat = ids.reshape(-1)
+    assert list(ge) == sorted(set(flat.tolist()))
+    for g, x in enumerate(ge):
+        ents = dst[gs[g]:gs[g + 1]]
+        assert np.all(flat[ents] == x) and np.all(np.diff(ents) > 0)
+    assert np.array_equal(tok, dst // K)
+    bounds, d2, src, inv, mx = O.dispatch(ids, E)
+    assert bounds[-1] == T * K and mx == np.bincount(flat, minlength=E).max()
+    assert np.array_equal(np.sort(d2), np.arange(T * K))
+    assert np.array_equal(inv[d2], np.arange(T * K))
+    order = np.lexsort((np.arange(T * K), flat))
+    assert np.array_equal(d2, order)
+    assert np.array_equal(src, d2 // K)
+
+
+def test_layer_oracle_small():
+    """The whole block on a tiny Qwen-shaped layer: parts and combine agree with a float64 dequantised restatement."""
+    cfg = dict(synth.QWEN, n_expert=32, n_used=4)
+    layer = synth.make_layer(cfg, seed=0)
+    rng = np.random.default_rng(0)
+    h = synth.rms_normed(rng, 2, cfg["n_embd"])
+    out = O.moe_layer(layer, h, threads=4)
+    assert out["parts"].shape == (2, 4, cfg["n_embd"]) and np.all(np.isfinite(out["out"]))
+    xq = out["xq"]
+    d, _, codes = O.q8_1_unpack(xq)
+    xv = (d[..., None] * codes).reshape(2, -1).astype(np.float64)
+    L = synth.blob_layout(cfg)
+    t, k = 1, 2
+    e = out["ids"][t, k]
+    blob = layer["blobs"][e]
+    H, F = cfg["n_embd"], cfg["n_ff"]
+    G = deq_rows(cfg["gu_type"], blob[:L["up_off"]], F, H)
+    U = deq_rows(cfg["gu_type"], blob[L["up_off"]:L["down_off"]], F, H)
+    g, u = G @ xv[t], U @ xv[t]
+    hh = g / (1 + np.exp(-g)) * u
+    D = deq_rows(cfg["d_type"], blob[L["down_off"]:], H, F)
+    y = D @ hh
+    ref = out["parts"][t, k].astype(np.float64)
+    rel = np.linalg.norm(ref - y) / np.linalg.norm(y)
+    assert rel < 2e-2, rel   # q8_1 of the hidden layer and IQ3_XXS's integer truncation against exact float math

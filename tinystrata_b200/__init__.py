@@ -1,0 +1,248 @@
+"""tinystrata_b200 - TinyStrata's MoE expert-layer path on B200 (sm_100a).
+
+The product is ``libtsb_moe.so`` (C ABI in include/tsb_moe.h).  This module is the host-side mirror of the reference's
+expert-layer entry points over that ABI (same names, argument meaning and error behaviour: a failing call raises
+``TsbError`` where the reference throws or exits), taking torch CUDA tensors for device memory and streams.  There is no
+CPU fallback: without the built library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libtsb_moe.so")
+
+T_Q4_0, T_Q8_0, T_Q4_K, T_Q6_K, T_IQ3_XXS, T_IQ3_S = 2, 8, 12, 14, 18, 21
+ACT_SWIGLU, ACT_GELU_TANH, ACT_SWIGLU_CLAMP = 0, 1, 2
+Q8_1_BYTES = 36
+
+
+class TsbError(RuntimeError):
+    pass
+
+
+class ExpertLayout(C.Structure):
+    """tsb_expert_layout (the reference's NativeExpertLayout, iq_kernels.hpp:45-53)."""
+    _fields_ = [("gu_type", C.c_int32), ("d_type", C.c_int32), ("n_embd", C.c_int64), ("n_ff", C.c_int64),
+                ("gu_row", C.c_uint64), ("d_row", C.c_uint64), ("up_off", C.c_uint64), ("down_off", C.c_uint64),
+                ("bytes", C.c_uint64)]
+
+
+_lib = None
+_lock = threading.Lock()
+_p, _i32, _i64, _u64, _f = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_float
+
+# name -> (restype, argtypes); every symbol of include/tsb_moe.h
+SIGNATURES = {
+    "tsb_moe_abi_version": (C.c_int, []),
+    "tsb_last_error": (C.c_char_p, []),
+    "tsb_device_error": (C.c_int, [C.POINTER(C.c_uint), C.c_int]),
+    "tsb_type_supported": (C.c_int, [C.c_int]),
+    "tsb_row_bytes": (_i64, [C.c_int, _i64]),
+    "tsb_native_expert_layout": (C.c_int, [C.c_int, C.c_int, _i64, _i64, C.POINTER(ExpertLayout)]),
+    "tsb_native_expert_supported": (C.c_int, [C.c_int, C.c_int, _i64, _i64]),
+    "tsb_native_expert_scratch_bytes": (_u64, [_i64, _i64]),
+    "tsb_quantize_q8_1_rows": (C.c_int, [_p, _i64, _i64, _p, _p]),
+    "tsb_router_logits_f32": (C.c_int, [_p, _p, _p, C.c_int, C.c_int, C.c_int, C.c_int, _p]),
+    "tsb_native_router_topk": (C.c_int, [_p, _p, _p, C.c_int, C.c_int, C.c_int, C.c_int, _p]),
+    "tsb_route_rows": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, C.c_int, _f, _p, _p, C.c_int, _f, _p, _p, _p]),
+    "tsb_moe_group": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, _p, _u64, _p, _p, _p, _p, _p, _p]),
+    "tsb_native_expert_grouped": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p, _p,
+                                            _i64]),
+    "tsb_native_expert_grouped_act": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
+                                                C.c_int, _f, _p]),
+    "tsb_moe_combine": (C.c_int, [_p, _p, _p, _p, C.c_int, _p, _p, C.c_int, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
+    "tsb_moe_sum": (C.c_int, [_p, _p, _p, C.c_int, C.c_int, C.c_int, _p]),
+    "tsb_rms_norm_q8_1": (C.c_int, [_p, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
+    "tsb_native_expert_set_phase": (C.c_int, [C.c_int]),
+    "tsb_debug_row_calls": (C.c_int, [C.c_int, _p, _p, _i64, _p, _p, _p]),
+}
+
+
+def lib():
+    """The loaded libtsb_moe.so (raises when it has not been built: there is no fallback)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise TsbError(f"{LIB_PATH} is missing: run `python -m tinystrata_b200.build` (no CPU fallback)")
+            L = C.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name, None)
+                if fn is None:
+                    continue
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().tsb_last_error().decode()
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        raise TsbError(f"{what}: status {rc}: {last_error()}")
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+# ------------------------------------------------------------------------------------------------ formats
+def row_bytes(ggml_type: int, n: int) -> int:
+    return int(lib().tsb_row_bytes(ggml_type, n))
+
+
+def native_expert_layout(gu_type: int, d_type: int, n_embd: int, n_ff: int) -> ExpertLayout:
+    L = ExpertLayout()
+    _check(lib().tsb_native_expert_layout(gu_type, d_type, n_embd, n_ff, C.byref(L)), "native_expert_layout")
+    return L
+
+
+def native_expert_supported(gu_type, d_type, n_embd, n_ff) -> bool:
+    return bool(lib().tsb_native_expert_supported(gu_type, d_type, n_embd, n_ff))
+
+
+def native_expert_scratch_bytes(cap_entries: int, n_ff: int) -> int:
+    return int(lib().tsb_native_expert_scratch_bytes(cap_entries, n_ff))
+
+
+# ------------------------------------------------------------------------------------------------ entry points
+def quantize_q8_1_rows(x, y=None, stream=None):
+    """fp32 [rows, n] -> q8_1 uint8 [rows, n / 32 * 36] (quantize_q8_1_rows, iq_kernels.hpp:24)."""
+    import torch
+    rows, n = x.shape
+    if y is None:
+        y = torch.empty((rows, n // 32 * Q8_1_BYTES), dtype=torch.uint8, device=x.device)
+    _check(lib().tsb_quantize_q8_1_rows(_ptr(x), rows, n, _ptr(y), _stream(stream)), "quantize_q8_1_rows")
+    return y
+
+
+def router_logits_f32(W, h, logits=None, ld=None, stream=None):
+    import torch
+    n_out, n_in = W.shape
+    T = h.shape[0]
+    ld = ld or n_out
+    if logits is None:
+        logits = torch.empty((T, ld), dtype=torch.float32, device=h.device)
+    _check(lib().tsb_router_logits_f32(_ptr(W), _ptr(h), _ptr(logits), n_in, n_out, T, ld, _stream(stream)),
+           "router_logits_f32")
+    return logits
+
+
+def native_router_topk(logits, k: int, n_expert: int | None = None, ids=None, w=None, stream=None):
+    """Softmax top-k (native_router_topk, native_router.hpp:5-6); logits [T, ld >= n_expert]."""
+    import torch
+    T, ld = logits.shape
+    n_expert = n_expert or ld
+    ids = ids if ids is not None else torch.empty((T, k), dtype=torch.int32, device=logits.device)
+    w = w if w is not None else torch.empty((T, k), dtype=torch.float32, device=logits.device)
+    _check(lib().tsb_native_router_topk(_ptr(logits), _ptr(ids), _ptr(w), n_expert, k, T, ld, _stream(stream)),
+           "native_router_topk")
+    return ids, w
+
+
+def route_rows(logits, n_used, gate, in_scale=1.0, bias=None, escale=None, norm=True, w_scale=0.0, stream=None):
+    """Gemma 4 / LFM2 routing (route_rows, gemma4/kernels.cu:289-356)."""
+    import torch
+    rows, E = logits.shape
+    ids = torch.empty((rows, n_used), dtype=torch.int32, device=logits.device)
+    w = torch.empty((rows, n_used), dtype=torch.float32, device=logits.device)
+    _check(lib().tsb_route_rows(_ptr(logits), E, n_used, rows, gate, in_scale, _ptr(bias), _ptr(escale), int(norm),
+                                w_scale, _ptr(ids), _ptr(w), _stream(stream)), "route_rows")
+    return ids, w
+
+
+class Groups:
+    """Device group tables (k_group's outputs) for up to cap entries."""
+
+    def __init__(self, cap_entries: int, device):
+        import torch
+        self.cap = cap_entries
+        self.grp_ptr = torch.zeros(cap_entries, dtype=torch.int64, device=device)
+        self.grp_start = torch.zeros(cap_entries + 1, dtype=torch.int32, device=device)
+        self.n_groups = torch.zeros(1, dtype=torch.int32, device=device)
+        self.ent_dst = torch.zeros(cap_entries, dtype=torch.int32, device=device)
+        self.ent_tok = torch.zeros(cap_entries, dtype=torch.int32, device=device)
+
+
+def moe_group(ids, n_expert: int, blobs, blob_stride: int, groups: Groups | None = None, stream=None) -> Groups:
+    """Decode grouping (k_group, q36_engine.cu:396-422); blobs = device base of the layer's expert blobs."""
+    T, K = ids.shape
+    groups = groups or Groups(T * K, ids.device)
+    base = blobs.data_ptr() if hasattr(blobs, "data_ptr") else int(blobs)
+    _check(lib().tsb_moe_group(_ptr(ids), T * K, K, n_expert, C.c_void_p(base), blob_stride, _ptr(groups.grp_ptr),
+                               _ptr(groups.grp_start), _ptr(groups.n_groups), _ptr(groups.ent_dst),
+                               _ptr(groups.ent_tok), _stream(stream)), "moe_group")
+    return groups
+
+
+def native_expert_grouped(L: ExpertLayout, groups: Groups, cap_groups: int, cap_entries: int, x_q8_1, scratch, out,
+                          act: int = ACT_SWIGLU, limit: float = float("inf"), stream=None):
+    """Grouped experts (native_expert_grouped, iq_kernels.hpp:75-78); act selects the Gemma/LFM activations."""
+    args = (C.byref(L), _ptr(groups.grp_ptr), _ptr(groups.grp_start), _ptr(groups.n_groups), _ptr(groups.ent_dst),
+            _ptr(groups.ent_tok), cap_groups, cap_entries, _ptr(x_q8_1), _ptr(scratch), _ptr(out))
+    if act == ACT_SWIGLU:
+        _check(lib().tsb_native_expert_grouped(*args, _stream(stream), 0), "native_expert_grouped")
+    else:
+        _check(lib().tsb_native_expert_grouped_act(*args, act, limit, _stream(stream)), "native_expert_grouped_act")
+    return out
+
+
+def moe_combine(x, parts, wts, K, shared=None, sgate=None, sg_stride=1, prow=None, wn=None, h=None, hq=None,
+                eps=1e-6, stream=None):
+    """x += sum_k w part + sigmoid(sgate) shared; h = rms(x) wn; hq = q8_1(h) (k_moe_out, q36_engine.cu:307-332)."""
+    T, n = x.shape
+    _check(lib().tsb_moe_combine(_ptr(x), _ptr(parts), _ptr(prow), _ptr(wts), K, _ptr(shared), _ptr(sgate), sg_stride,
+                                 _ptr(wn), _ptr(h), _ptr(hq), n, eps, T, _stream(stream)), "moe_combine")
+    return x
+
+
+def rms_norm_q8_1(x, h=None, hq=None, wn=None, eps=1e-6, stream=None):
+    """h = rms(x) * wn and its q8_1 image (the layer input's norm, q36_kernels.cuh:222-250 without the add)."""
+    T_, n = x.shape
+    _check(lib().tsb_rms_norm_q8_1(_ptr(x), _ptr(wn), _ptr(h), _ptr(hq), n, eps, T_, _stream(stream)), "rms_norm_q8_1")
+
+
+def native_expert_set_phase(phase: int):
+    _check(lib().tsb_native_expert_set_phase(phase), "native_expert_set_phase")
+
+
+def moe_sum(x, w, acc, n_used, stream=None):
+    rows, n = acc.shape
+    _check(lib().tsb_moe_sum(_ptr(x), _ptr(w), _ptr(acc), n, n_used, rows, _stream(stream)), "moe_sum")
+    return acc
+
+
+def debug_row_calls(ggml_type: int, row, x_q8_1, n: int, stream=None):
+    import torch
+    qk = {T_Q4_0: 32, T_Q8_0: 32, T_Q4_K: 256, T_Q6_K: 256, T_IQ3_XXS: 256, T_IQ3_S: 256}[ggml_type]
+    cpb = {T_Q4_0: 2, T_Q8_0: 4, T_Q4_K: 16, T_Q6_K: 32, T_IQ3_XXS: 8, T_IQ3_S: 8}[ggml_type]
+    calls = n // qk * cpb
+    s = torch.empty(calls, dtype=torch.int32, device=row.device)
+    v = torch.empty(calls, dtype=torch.float32, device=row.device)
+    _check(lib().tsb_debug_row_calls(ggml_type, _ptr(row), _ptr(x_q8_1), n, _ptr(s), _ptr(v), _stream(stream)),
+           "debug_row_calls")
+    return s, v
+
+
+def device_error(clear: bool = True) -> int:
+    code = C.c_uint(0)
+    _check(lib().tsb_device_error(C.byref(code), int(clear)), "device_error")
+    return int(code.value)
+
+
+from .layer import MoELayer  # noqa: E402  (host mirror of the engines' MoE block)

@@ -1,0 +1,758 @@
+// tsb_moe.cu - the B200 MoE expert path behind TinyStrata's expert-layer entry points: q8_1 quantiser, router GEMV,
+// softmax / sigmoid top-k routers, decode grouping, grouped expert GEMVs, combine.  The C ABI is include/tsb_moe.h.
+#include "tsb_kernels.cuh"
+#include "../../include/tsb_moe.h"
+
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace tsb {
+
+// ================================================================================================ host error state
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+static int cuda_status(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(TSB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return TSB_OK;
+}
+static inline cudaStream_t cs(void* s) { return (cudaStream_t) s; }
+static bool aligned(const void* p, size_t a) { return ((uintptr_t) p % a) == 0; }
+
+struct DevInfo {
+    int sms = 0;
+    unsigned* err = nullptr;   // device error word (bounded waits that gave up)
+};
+static DevInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+static DevInfo* dev_info() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo& I = g_dev[d];
+    if (I.sms == 0) {
+        cudaDeviceGetAttribute(&I.sms, cudaDevAttrMultiProcessorCount, d);
+        if (cudaMalloc(&I.err, sizeof(unsigned)) != cudaSuccess) return nullptr;
+        cudaMemset(I.err, 0, sizeof(unsigned));
+    }
+    return &I;
+}
+
+// ================================================================================================ formats (host)
+static int qk_of(int t) {
+    switch (t) {
+        case T_Q4_0: case T_Q8_0: return 32;
+        case T_Q4_K: case T_Q6_K: case T_IQ3_XXS: case T_IQ3_S: return 256;
+        default: return 0;
+    }
+}
+static int bb_of(int t) {
+    switch (t) {
+        case T_Q4_0: return 18;
+        case T_Q8_0: return 34;
+        case T_Q4_K: return 144;
+        case T_Q6_K: return 210;
+        case T_IQ3_XXS: return 98;
+        case T_IQ3_S: return 110;
+        default: return 0;
+    }
+}
+static int cpb_of(int t) {
+    switch (t) {
+        case T_Q4_0: return 2;
+        case T_Q8_0: return 4;
+        case T_Q4_K: return 16;
+        case T_Q6_K: return 32;
+        case T_IQ3_XXS: case T_IQ3_S: return 8;
+        default: return 0;
+    }
+}
+
+// ================================================================================================ small kernels
+// q8_1 of rows (iq_kernels.cu:1483-1494): one warp per block, lane = value.
+__global__ void k_quantize_q8_1(const float* __restrict__ x, BlockQ8_1* __restrict__ y, long long n) {
+    const long long i = (long long) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i - (threadIdx.x & 31) >= n) return;   // whole warps only (n is a multiple of 32)
+    float d, sum;
+    const int8_t q = q8_1_warp(x[i], d, sum);
+    BlockQ8_1* b = y + i / 32;
+    b->qs[i % 32] = q;
+    if ((i % 32) == 0) b->ds = make_half2(__float2half(q8_finite(d)), __float2half(q8_finite(sum)));
+}
+
+// fp32 router logits: logits[t * ld + o] = W[o] . h[t] (the router GEMV, q36_engine.cu:2106-2131).  Warp per row,
+// float4 loads, up to 16 tokens per pass.
+__global__ void __launch_bounds__(256) k_router_logits(const float* __restrict__ W, const float* __restrict__ h,
+                                                       float* __restrict__ logits, int n_in, int n_out, int n_tok,
+                                                       int ld) {
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); o < n_out; o += warps) {
+        const float4* wr = (const float4*) (W + (size_t) o * n_in);
+        for (int t0 = 0; t0 < n_tok; t0 += 16) {
+            const int nt = min(16, n_tok - t0);
+            float acc[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[t] = 0.0f;
+            for (int i = lane; i < n_in / 4; i += 32) {
+                const float4 w = __ldg(wr + i);
+#pragma unroll
+                for (int t = 0; t < 16; ++t)
+                    if (t < nt) {
+                        const float4 x = __ldg((const float4*) (h + (size_t) (t0 + t) * n_in) + i);
+                        acc[t] += w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
+                    }
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+                if (t < nt) {
+                    const float v = warp_sum(acc[t]);
+                    if (lane == 0) logits[(size_t) (t0 + t) * ld + o] = v;
+                }
+        }
+    }
+}
+
+// Softmax top-k (native_router.cu:44-95, the same expressions under the reference's fast-math): a warp per token,
+// V = n_expert / 32 values a lane, lowest id first among equal probabilities, weights renormalised with the
+// 6.103515625e-5 floor.
+template <int V>
+__global__ void __launch_bounds__(256) k_route_topk(const float* __restrict__ logits, int ld, int32_t* __restrict__ ids,
+                                                    float* __restrict__ weights, int n_tok, int K) {
+    const int tk = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (tk >= n_tok) return;
+    const int lane = threadIdx.x & 31;
+    const float* lg = logits + (size_t) tk * ld;
+    ids += (size_t) tk * K;
+    weights += (size_t) tk * K;
+    float values[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) values[i] = lg[lane + i * 32];
+    float maximum = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < V; ++i) maximum = fmaxf(maximum, values[i]);
+    maximum = warp_max(maximum);
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        values[i] = fexp_fm(values[i] - maximum);
+        sum += values[i];
+    }
+    const float reciprocal = frcp_fm(warp_sum(sum));
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        values[i] *= reciprocal;
+        if (__isnanf(values[i])) values[i] = -FLT_MAX;
+    }
+    float selected = 0.0f, selected_sum = 0.0f;
+    for (int rank = 0; rank < K; ++rank) {
+        float best = values[0];
+        int expert = lane;
+#pragma unroll
+        for (int i = 1; i < V; ++i)
+            if (values[i] > best) {
+                best = values[i];
+                expert = lane + i * 32;
+            }
+#pragma unroll
+        for (int m = 16; m; m >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, m);
+            const int oi = __shfl_xor_sync(0xffffffffu, expert, m);
+            if (ob > best || (ob == best && oi < expert)) {
+                best = ob;
+                expert = oi;
+            }
+        }
+        if ((expert & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < V; ++i)
+                if (i == expert / 32) values[i] = -INFINITY;
+            ids[rank] = expert;
+            selected_sum += best;
+        }
+        if (rank == lane) selected = best;
+    }
+    selected_sum = fmaxf(warp_sum(selected_sum), 6.103515625e-5f);
+    const float inv = frcp_fm(selected_sum);
+    if (lane < K) weights[lane] = selected * inv;
+}
+
+// Gemma / LFM routing (route_kernel, gemma4/kernels.cu:289-356; that file is built without fast-math): gate 0 softmax
+// of logit * in_scale, gate 1 sigmoid; pick on p + bias (lowest id on ties); w = p [/ max(sum, floor)] [* escale]
+// [* w_scale].  A warp per token, PER experts a lane.
+template <int PER>
+__global__ void __launch_bounds__(256) k_route_rows(const float* __restrict__ logits, int n_expert, int n_used, int rows,
+                                                    int gate, float in_scale, const float* __restrict__ bias,
+                                                    const float* __restrict__ escale, int norm, float w_scale,
+                                                    int32_t* __restrict__ ids, float* __restrict__ w) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* lg = logits + (size_t) row * n_expert;
+    float p[PER], pick[PER];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int e = lane + k * 32;
+        p[k] = e < n_expert ? lg[e] * in_scale : -INFINITY;
+        mx = fmaxf(mx, p[k]);
+    }
+    if (gate == 0) {
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            p[k] = lane + k * 32 < n_expert ? expf(p[k] - mx) : 0.0f;
+            sum += p[k];
+        }
+        const float inv = __fdiv_rn(1.0f, warp_sum(sum));
+#pragma unroll
+        for (int k = 0; k < PER; ++k) p[k] *= inv;
+    } else {
+#pragma unroll
+        for (int k = 0; k < PER; ++k) p[k] = __fdiv_rn(1.0f, 1.0f + expf(-p[k]));
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int e = lane + k * 32;
+        pick[k] = e < n_expert ? p[k] + (bias ? bias[e] : 0.0f) : -INFINITY;
+    }
+    float sum = 0.0f, mine = 0.0f;
+    int my_id = 0;
+    for (int j = 0; j < n_used; ++j) {
+        float best = -INFINITY;
+        int at = n_expert;
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (pick[k] > best) best = pick[k], at = lane + k * 32;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float b = __shfl_xor_sync(0xffffffffu, best, o);
+            const int a = __shfl_xor_sync(0xffffffffu, at, o);
+            if (b > best || (b == best && a < at)) best = b, at = a;
+        }
+        float pw = 0.0f;
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (lane + k * 32 == at) pw = p[k], pick[k] = -INFINITY;
+        pw = __shfl_sync(0xffffffffu, pw, at % 32);
+        sum += pw;
+        if (lane == j) mine = pw, my_id = at;
+    }
+    if (lane >= n_used) return;
+    float v = mine;
+    if (norm) v = __fdiv_rn(v, fmaxf(sum, 6.103515625e-5f));
+    if (escale) v *= escale[my_id];
+    if (w_scale != 0.0f) v *= w_scale;
+    ids[(size_t) row * n_used + lane] = my_id;
+    w[(size_t) row * n_used + lane] = v;
+}
+
+// Decode grouping (k_group, q36_engine.cu:396-422): groups of ascending expert id, entries in entry order.  One CTA;
+// an entry's slot is the number of entries before it in (expert, entry) order.
+__global__ void __launch_bounds__(1024) k_group(const int32_t* __restrict__ ids, int n_ent, int K, int n_expert,
+                                                const uint8_t* blobs, unsigned long long stride,
+                                                unsigned long long* grp_ptr, int32_t* grp_start, int32_t* n_groups,
+                                                int32_t* ent_dst, int32_t* ent_tok) {
+    extern __shared__ int sh[];
+    int* cnt = sh;                 // n_expert
+    int* off = sh + n_expert;      // n_expert + 1 (exclusive scan)
+    int* gidx = off + n_expert + 1;  // n_expert: group index of an expert
+    for (int x = threadIdx.x; x < n_expert; x += blockDim.x) cnt[x] = 0;
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_ent; e += blockDim.x) atomicAdd(&cnt[ids[e]], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int pos = 0, g = 0;
+        for (int x = 0; x < n_expert; ++x) {
+            off[x] = pos;
+            gidx[x] = g;
+            if (cnt[x]) {
+                grp_ptr[g] = (unsigned long long) (blobs + (size_t) x * stride);
+                grp_start[g] = pos;
+                ++g;
+            }
+            pos += cnt[x];
+        }
+        off[n_expert] = pos;
+        grp_start[g] = pos;
+        *n_groups = g;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_ent; e += blockDim.x) {
+        const int id = ids[e];
+        int before = 0;
+        for (int e2 = 0; e2 < e; ++e2) before += ids[e2] == id;
+        const int p = off[id] + before;
+        ent_dst[p] = e;
+        ent_tok[p] = e / K;
+    }
+}
+
+// Combine (k_moe_out / k_moe_out_small, q36_engine.cu:307-332, q36_kernels.cuh:252-290): x += w0 p0 (+ fmaf over the
+// picks in order) + sigmoid(sgate) shared; then with wn: h = rms(x) wn and hq = q8_1(h).  One CTA of 1024 per token; the
+// squares are summed per 256-thread slot (element s, s + 256, ...) then the 256-wide tree, as the reference.
+__global__ void __launch_bounds__(1024) k_combine(float* __restrict__ x, const float* __restrict__ parts,
+                                                  const int32_t* __restrict__ prow, const float* __restrict__ wts, int K,
+                                                  const float* __restrict__ shared, const float* __restrict__ sgate,
+                                                  int sg_stride, const float* __restrict__ wn, float* __restrict__ h,
+                                                  BlockQ8_1* __restrict__ hq, int n, float eps) {
+    extern __shared__ float vv[];   // n values of x, then 256 partial sums
+    float* sh = vv + n;
+    __shared__ const float* pk[32];
+    const int t = blockIdx.x;
+    float* xr = x + (size_t) t * n;
+    if ((int) threadIdx.x < K)
+        pk[threadIdx.x] = parts + (size_t) (prow ? prow[t * K + threadIdx.x] : t * K + threadIdx.x) * n;
+    __syncthreads();
+    const float* wr = wts + (size_t) t * K;
+    // sigmoid and the mean under the reference engine's fast-math build (CMakeLists.txt:204-207)
+    const float gs = sgate ? frcp_fm(1.0f + fexp_fm(-sgate[(size_t) t * sg_stride])) : 1.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float acc = wr[0] * pk[0][i];
+        for (int k = 1; k < K; ++k) acc = fmaf(wr[k], pk[k][i], acc);
+        if (shared) acc += gs * shared[(size_t) t * n + i];
+        const float v = xr[i] + acc;
+        xr[i] = v;
+        vv[i] = v;
+    }
+    if (wn == nullptr && h == nullptr) return;
+    __syncthreads();
+    if (threadIdx.x < 256) {
+        float s = 0.0f;
+        for (int i = threadIdx.x; i < n; i += 256) s += vv[i] * vv[i];
+        sh[threadIdx.x] = s;
+    }
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if ((int) threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+        __syncthreads();
+    }
+    const float r = rsqrtf(fdiv_fm(sh[0], (float) n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float hv = __fmul_rn(__fmul_rn(vv[i], r), wn ? wn[i] : 1.0f);
+        if (h) h[(size_t) t * n + i] = hv;
+        if (hq) {
+            float d, sum;
+            const int8_t q = q8_1_warp(hv, d, sum);
+            BlockQ8_1* b = hq + (size_t) t * (n >> 5) + (i >> 5);
+            b->qs[i & 31] = q;
+            if ((i & 31) == 0) b->ds = make_half2(__float2half(q8_finite(d)), __float2half(q8_finite(sum)));
+        }
+    }
+}
+
+// h = x * rsqrt(mean(x^2) + eps) * wn and hq = q8_1(h), one CTA of 1024 per row: the combine's epilogue alone (the
+// reference's k_add_rms_q without the add, q36_kernels.cuh:222-250).
+__global__ void __launch_bounds__(1024) k_rms_q8_1(const float* __restrict__ x, const float* __restrict__ wn,
+                                                   float* __restrict__ h, BlockQ8_1* __restrict__ hq, int n, float eps) {
+    __shared__ float sh[256];
+    const float* xr = x + (size_t) blockIdx.x * n;
+    if (threadIdx.x < 256) {
+        float s = 0.0f;
+        for (int i = threadIdx.x; i < n; i += 256) s += xr[i] * xr[i];
+        sh[threadIdx.x] = s;
+    }
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if ((int) threadIdx.x < s) sh[threadIdx.x] += sh[threadIdx.x + s];
+        __syncthreads();
+    }
+    const float r = rsqrtf(fdiv_fm(sh[0], (float) n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float hv = __fmul_rn(__fmul_rn(xr[i], r), wn ? wn[i] : 1.0f);
+        if (h) h[(size_t) blockIdx.x * n + i] = hv;
+        if (hq) {
+            float d, sum;
+            const int8_t q = q8_1_warp(hv, d, sum);
+            BlockQ8_1* b = hq + (size_t) blockIdx.x * (n >> 5) + (i >> 5);
+            b->qs[i & 31] = q;
+            if ((i & 31) == 0) b->ds = make_half2(__float2half(q8_finite(d)), __float2half(q8_finite(sum)));
+        }
+    }
+}
+
+// Gemma / LFM ordered weighted sum (moe_sum, gemma4/kernels.cu:358-366): acc[t] += sum_k w[t,k] x[t*K+k].
+__global__ void k_moe_sum(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ acc, int n,
+                          int n_used) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const size_t first = (size_t) blockIdx.y * n_used;
+    float s = 0.0f;
+    for (int k = 0; k < n_used; ++k) s += w[first + k] * x[(first + k) * n + i];
+    acc[(size_t) blockIdx.y * n + i] += s;
+}
+
+// Test hook: the per-call integer sums and float values of one row against one q8_1 activation.
+template <int TY>
+__global__ void k_row_calls(const uint8_t* __restrict__ row, const BlockQ8_1* __restrict__ x, int n_calls,
+                            int32_t* __restrict__ sumi, float* __restrict__ val, int row_bytes) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int TB = table_bytes<TY>();
+    build_tables<TY>(smem);
+    uint8_t* rs = smem + TB;
+    for (int i = threadIdx.x; i < row_bytes; i += blockDim.x) rs[i] = row[i];
+    __syncthreads();
+    const IqTab tab = make_tab(smem, threadIdx.x & 31);
+    auto src = [&](int blk) { return qb_from_global(x + blk); };
+    for (int k = threadIdx.x; k < n_calls; k += blockDim.x) {
+        const typename Fmt<TY>::Act a = Fmt<TY>::act(src, k);
+        const typename Fmt<TY>::W w = decode_call<TY>(rs, k, tab);
+        sumi[k] = Fmt<TY>::sumi(w, a);
+        val[k] = Fmt<TY>::apply(w, a);
+    }
+}
+
+// ================================================================================================ expert launches
+// Bench-only phase selection, as the reference's native_expert_set_mode (iq_kernels.hpp:85): 0 both kernels,
+// 1 gate/up + activation only, 2 down only.
+static int g_phase = 0;
+template <int TY, int J>
+static int launch_gu_t(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const void* xq, float* h,
+                       int act, float limit, cudaStream_t s, DevInfo* di) {
+    GuParams p;
+    p.g = g;
+    p.xq = (const BlockQ8_1*) xq;
+    p.n_embd = (int) L->n_embd;
+    p.n_ff = (int) L->n_ff;
+    p.gu_row = L->gu_row;
+    p.up_off = L->up_off;
+    p.h = h;
+    p.act = act;
+    p.limit = limit;
+    p.err = di->err;
+    const uint32_t sb = (uint32_t) (2 * L->gu_row);
+    const size_t smem = expert_smem<TY>(sb);
+    auto kern = k_expert_gu<TY, J, 4>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
+        return cuda_status("expert gate/up: shared memory");
+    const long long tasks = (long long) cap_groups * L->n_ff;
+    const long long ctas = std::min<long long>((long long) di->sms * 2, (tasks + kWarps - 1) / kWarps);
+    kern<<<(unsigned) std::max<long long>(ctas, 1), kWarps * 32, smem, s>>>(p);
+    return cuda_status("expert gate/up");
+}
+
+template <int TY, int J>
+static int launch_down_t(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const float* h, float* out,
+                         cudaStream_t s, DevInfo* di) {
+    DownParams p;
+    p.g = g;
+    p.h = h;
+    p.n_embd = (int) L->n_embd;
+    p.n_ff = (int) L->n_ff;
+    p.d_row = L->d_row;
+    p.down_off = L->down_off;
+    int R = 1;
+    while ((R * L->d_row) % 16 != 0) R *= 2;
+    const int C = (int) (L->n_ff / qk_of(TY) * cpb_of(TY));
+    const int P = C < 32 ? 32 / C : 1;
+    while (R < P) R *= 2;
+    if (L->n_embd % R != 0) return fail(TSB_ERR_UNSUPPORTED, "down rows: n_embd %% %d", R);
+    p.R = R;
+    p.out = out;
+    p.err = di->err;
+    const uint32_t sb = (uint32_t) (R * L->d_row);
+    const size_t smem = expert_smem<TY>(sb);
+    auto kern = k_expert_down<TY, J, 4>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
+        return cuda_status("expert down: shared memory");
+    const long long tasks = (long long) cap_groups * (L->n_embd / R);
+    const long long ctas = std::min<long long>((long long) di->sms * 2, (tasks + kWarps - 1) / kWarps);
+    kern<<<(unsigned) std::max<long long>(ctas, 1), kWarps * 32, smem, s>>>(p);
+    return cuda_status("expert down");
+}
+
+// J = calls per lane for C calls per row (1, 2, 4, 8 instantiated)
+template <int TY>
+static int launch_gu(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const void* xq, float* h,
+                     int act, float limit, cudaStream_t s, DevInfo* di) {
+    const int C = (int) (L->n_embd / qk_of(TY) * cpb_of(TY));
+    const int J = (C + 31) / 32;
+    if (J <= 1) return launch_gu_t<TY, 1>(L, g, cap_groups, xq, h, act, limit, s, di);
+    if (J <= 2) return launch_gu_t<TY, 2>(L, g, cap_groups, xq, h, act, limit, s, di);
+    if (J <= 4) return launch_gu_t<TY, 4>(L, g, cap_groups, xq, h, act, limit, s, di);
+    if (J <= 8) return launch_gu_t<TY, 8>(L, g, cap_groups, xq, h, act, limit, s, di);
+    return fail(TSB_ERR_UNSUPPORTED, "gate/up: %d calls per row (at most 256)", C);
+}
+template <int TY>
+static int launch_down(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const float* h, float* out,
+                       cudaStream_t s, DevInfo* di) {
+    const int C = (int) (L->n_ff / qk_of(TY) * cpb_of(TY));
+    if (C < 32 && (C & (C - 1)) != 0) return fail(TSB_ERR_UNSUPPORTED, "down: %d calls per row", C);
+    const int J = (C + 31) / 32;
+    if (J <= 1) return launch_down_t<TY, 1>(L, g, cap_groups, h, out, s, di);
+    if (J <= 2) return launch_down_t<TY, 2>(L, g, cap_groups, h, out, s, di);
+    if (J <= 4) return launch_down_t<TY, 4>(L, g, cap_groups, h, out, s, di);
+    if (J <= 8) return launch_down_t<TY, 8>(L, g, cap_groups, h, out, s, di);
+    return fail(TSB_ERR_UNSUPPORTED, "down: %d calls per row (at most 256)", C);
+}
+
+static int gu_dispatch(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const void* xq, float* h,
+                       int act, float limit, cudaStream_t s, DevInfo* di) {
+    switch (L->gu_type) {
+        case T_IQ3_XXS: return launch_gu<T_IQ3_XXS>(L, g, cap_groups, xq, h, act, limit, s, di);
+        case T_IQ3_S: return launch_gu<T_IQ3_S>(L, g, cap_groups, xq, h, act, limit, s, di);
+        case T_Q4_0: return launch_gu<T_Q4_0>(L, g, cap_groups, xq, h, act, limit, s, di);
+        case T_Q8_0: return launch_gu<T_Q8_0>(L, g, cap_groups, xq, h, act, limit, s, di);
+        case T_Q4_K: return launch_gu<T_Q4_K>(L, g, cap_groups, xq, h, act, limit, s, di);
+        case T_Q6_K: return launch_gu<T_Q6_K>(L, g, cap_groups, xq, h, act, limit, s, di);
+        default: return fail(TSB_ERR_UNSUPPORTED, "gate/up type %d", L->gu_type);
+    }
+}
+static int down_dispatch(const tsb_expert_layout* L, const GroupArgs& g, int64_t cap_groups, const float* h, float* out,
+                         cudaStream_t s, DevInfo* di) {
+    switch (L->d_type) {
+        case T_IQ3_XXS: return launch_down<T_IQ3_XXS>(L, g, cap_groups, h, out, s, di);
+        case T_IQ3_S: return launch_down<T_IQ3_S>(L, g, cap_groups, h, out, s, di);
+        case T_Q4_0: return launch_down<T_Q4_0>(L, g, cap_groups, h, out, s, di);
+        case T_Q8_0: return launch_down<T_Q8_0>(L, g, cap_groups, h, out, s, di);
+        case T_Q4_K: return launch_down<T_Q4_K>(L, g, cap_groups, h, out, s, di);
+        case T_Q6_K: return launch_down<T_Q6_K>(L, g, cap_groups, h, out, s, di);
+        default: return fail(TSB_ERR_UNSUPPORTED, "down type %d", L->d_type);
+    }
+}
+
+}  // namespace tsb
+
+// ================================================================================================ C ABI
+using namespace tsb;
+
+extern "C" {
+
+int tsb_moe_abi_version(void) { return TSB_MOE_ABI_VERSION; }
+
+const char* tsb_last_error(void) { return g_err; }
+
+int tsb_device_error(unsigned* code, int clear) {
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    unsigned v = 0;
+    if (cudaMemcpy(&v, di->err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_status("device error");
+    if (clear) cudaMemset(di->err, 0, sizeof(unsigned));
+    if (code) *code = v;
+    return TSB_OK;
+}
+
+int tsb_type_supported(int ggml_type) { return qk_of(ggml_type) > 0; }
+
+int64_t tsb_row_bytes(int ggml_type, int64_t n) {
+    const int qk = qk_of(ggml_type);
+    if (qk == 0 || n % qk != 0) return -1;
+    return n / qk * bb_of(ggml_type);
+}
+
+int tsb_native_expert_layout(int gu_type, int d_type, int64_t n_embd, int64_t n_ff, tsb_expert_layout* L) {
+    if (!L) return fail(TSB_ERR_ARG, "layout: null output");
+    const int64_t gr = tsb_row_bytes(gu_type, n_embd), dr = tsb_row_bytes(d_type, n_ff);
+    if (gr <= 0 || dr <= 0) return fail(TSB_ERR_UNSUPPORTED, "layout: types %d/%d at %lld/%lld", gu_type, d_type,
+                                        (long long) n_embd, (long long) n_ff);
+    L->gu_type = gu_type;
+    L->d_type = d_type;
+    L->n_embd = n_embd;
+    L->n_ff = n_ff;
+    L->gu_row = (uint64_t) gr;
+    L->d_row = (uint64_t) dr;
+    L->up_off = (uint64_t) (n_ff * gr);
+    L->down_off = 2 * L->up_off;
+    L->bytes = L->down_off + (uint64_t) (n_embd * dr);
+    return TSB_OK;
+}
+
+int tsb_native_expert_supported(int gu_type, int d_type, int64_t n_embd, int64_t n_ff) {
+    tsb_expert_layout L;
+    if (tsb_native_expert_layout(gu_type, d_type, n_embd, n_ff, &L) != TSB_OK) return 0;
+    if (L.gu_row % 16 != 0 || n_ff % 32 != 0) return 0;
+    const int Cg = (int) (n_embd / qk_of(gu_type) * cpb_of(gu_type));
+    const int Cd = (int) (n_ff / qk_of(d_type) * cpb_of(d_type));
+    if (Cg > 256 || Cd > 256 || (Cd < 32 && (Cd & (Cd - 1)) != 0)) return 0;
+    return 1;
+}
+
+uint64_t tsb_native_expert_scratch_bytes(int64_t cap_entries, int64_t n_ff) {
+    return (uint64_t) ((cap_entries * n_ff * 4 + 255) & ~255LL);
+}
+
+int tsb_quantize_q8_1_rows(const float* x, int64_t n_rows, int64_t n_cols, void* y, void* stream) {
+    if (!x || !y || n_rows < 0 || n_cols % 32 != 0) return fail(TSB_ERR_ARG, "quantize_q8_1_rows: arguments");
+    const long long n = n_rows * n_cols;
+    if (n == 0) return TSB_OK;
+    k_quantize_q8_1<<<(unsigned) ((n + 255) / 256), 256, 0, cs(stream)>>>(x, (BlockQ8_1*) y, n);
+    return cuda_status("quantize_q8_1_rows");
+}
+
+int tsb_router_logits_f32(const float* W, const float* h, float* logits, int n_in, int n_out, int n_tok, int ld,
+                          void* stream) {
+    if (!W || !h || !logits || n_in % 4 != 0 || n_tok < 0 || ld < n_out || !aligned(W, 16) || !aligned(h, 16))
+        return fail(TSB_ERR_ARG, "router_logits_f32: arguments (n_in %% 4, 16-byte aligned W and h, ld >= n_out)");
+    if (n_tok == 0) return TSB_OK;
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    const int ctas = std::min((n_out + 7) / 8, di->sms * 4);
+    k_router_logits<<<ctas, 256, 0, cs(stream)>>>(W, h, logits, n_in, n_out, n_tok, ld);
+    return cuda_status("router_logits_f32");
+}
+
+int tsb_native_router_topk(const float* logits, int32_t* ids, float* weights, int n_expert, int k, int n_tok, int ld,
+                           void* stream) {
+    if (!logits || !ids || !weights || n_tok < 0 || k < 1 || k > 32 || n_expert % 32 != 0 || n_expert < 32 ||
+        n_expert > 512 || ld < n_expert || k > n_expert)
+        return fail(TSB_ERR_ARG, "native_router_topk: 32..512 experts (a multiple of 32), 1..32 picks");
+    if (n_tok == 0) return TSB_OK;
+    const unsigned grid = (unsigned) ((n_tok + 7) / 8);
+    switch (n_expert / 32) {
+#define TSB_V(v) case v: k_route_topk<v><<<grid, 256, 0, cs(stream)>>>(logits, ld, ids, weights, n_tok, k); break;
+        TSB_V(1) TSB_V(2) TSB_V(3) TSB_V(4) TSB_V(5) TSB_V(6) TSB_V(7) TSB_V(8)
+        TSB_V(9) TSB_V(10) TSB_V(11) TSB_V(12) TSB_V(13) TSB_V(14) TSB_V(15) TSB_V(16)
+#undef TSB_V
+    }
+    return cuda_status("native_router_topk");
+}
+
+int tsb_route_rows(const float* logits, int n_expert, int n_used, int rows, int gate, float in_scale, const float* bias,
+                   const float* escale, int norm, float w_scale, int32_t* ids, float* w, void* stream) {
+    if (rows <= 0) return TSB_OK;
+    if (!logits || !ids || !w || n_expert > 512 || n_expert < 1 || n_used < 1 || n_used > 32 || n_used > n_expert ||
+        (gate != 0 && gate != 1))
+        return fail(TSB_ERR_ARG, "route_rows: at most 512 experts and 32 picks, gate 0 (softmax) or 1 (sigmoid)");
+    const unsigned grid = (unsigned) ((rows + 7) / 8);
+    auto go = [&](auto kern) {
+        kern<<<grid, 256, 0, cs(stream)>>>(logits, n_expert, n_used, rows, gate, in_scale, bias, escale, norm, w_scale,
+                                           ids, w);
+    };
+    if (n_expert <= 64) go(k_route_rows<2>);
+    else if (n_expert <= 128) go(k_route_rows<4>);
+    else if (n_expert <= 256) go(k_route_rows<8>);
+    else go(k_route_rows<16>);
+    return cuda_status("route_rows");
+}
+
+int tsb_moe_group(const int32_t* ids, int n_ent, int K, int n_expert, const void* blobs, uint64_t blob_stride,
+                  uint64_t* grp_ptr, int32_t* grp_start, int32_t* n_groups, int32_t* ent_dst, int32_t* ent_tok,
+                  void* stream) {
+    if (!ids || !grp_ptr || !grp_start || !n_groups || !ent_dst || !ent_tok || K < 1 || n_ent < 0 || n_ent % K != 0 ||
+        n_expert < 1 || n_expert > 4096)
+        return fail(TSB_ERR_ARG, "moe_group: arguments");
+    const size_t sh = sizeof(int) * (3 * (size_t) n_expert + 1);
+    k_group<<<1, 1024, sh, cs(stream)>>>(ids, n_ent, K, n_expert, (const uint8_t*) blobs, blob_stride,
+                                         (unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok);
+    return cuda_status("moe_group");
+}
+
+int tsb_native_expert_grouped(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                              const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                              int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, void* scratch, float* out,
+                              void* stream, int64_t grid_groups) {
+    (void) grid_groups;   // the results never depend on it (iq_kernels.hpp:72-74); the launch is persistent anyway
+    if (cap_groups <= 0 || cap_entries <= 0) return TSB_OK;
+    if (!L || !grp_ptr || !grp_start || !n_groups || !ent_dst || !ent_tok || !x_q8_1 || !scratch || !out)
+        return fail(TSB_ERR_ARG, "native_expert_grouped: null argument");
+    if (!tsb_native_expert_supported(L->gu_type, L->d_type, L->n_embd, L->n_ff))
+        return fail(TSB_ERR_UNSUPPORTED, "native_expert_grouped: types %d/%d at %lld/%lld", L->gu_type, L->d_type,
+                    (long long) L->n_embd, (long long) L->n_ff);
+    if (L->up_off % 16 || L->down_off % 16 || L->bytes % 16)
+        return fail(TSB_ERR_ALIGN, "native_expert_grouped: blob offsets must be multiples of 16 bytes");
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    float* h = (float*) scratch;
+    if (g_phase != 2) {
+        const int rc = gu_dispatch(L, g, cap_groups, x_q8_1, h, ACT_SWIGLU, INFINITY, cs(stream), di);
+        if (rc != TSB_OK) return rc;
+    }
+    if (g_phase == 1) return TSB_OK;
+    return down_dispatch(L, g, cap_groups, h, out, cs(stream), di);
+}
+
+int tsb_native_expert_grouped_act(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                                  const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                                  int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, void* scratch,
+                                  float* out, int act, float limit, void* stream) {
+    if (cap_groups <= 0 || cap_entries <= 0) return TSB_OK;
+    if (!L || !grp_ptr || !grp_start || !n_groups || !ent_dst || !ent_tok || !x_q8_1 || !scratch || !out)
+        return fail(TSB_ERR_ARG, "native_expert_grouped_act: null argument");
+    if (act < 0 || act > 2) return fail(TSB_ERR_ARG, "native_expert_grouped_act: act 0 SwiGLU, 1 GELU-tanh, 2 clamped");
+    if (!tsb_native_expert_supported(L->gu_type, L->d_type, L->n_embd, L->n_ff))
+        return fail(TSB_ERR_UNSUPPORTED, "native_expert_grouped_act: unsupported layout");
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    float* h = (float*) scratch;
+    if (g_phase != 2) {
+        const int rc = gu_dispatch(L, g, cap_groups, x_q8_1, h, act, limit, cs(stream), di);
+        if (rc != TSB_OK) return rc;
+    }
+    if (g_phase == 1) return TSB_OK;
+    return down_dispatch(L, g, cap_groups, h, out, cs(stream), di);
+}
+
+int tsb_native_expert_set_phase(int phase) {
+    if (phase < 0 || phase > 2) return fail(TSB_ERR_ARG, "native_expert_set_phase: 0, 1 or 2");
+    g_phase = phase;
+    return TSB_OK;
+}
+
+int tsb_moe_combine(float* x, const float* parts, const int32_t* prow, const float* wts, int K, const float* shared,
+                    const float* sgate, int sg_stride, const float* wn, float* h, void* hq, int n, float eps, int n_tok,
+                    void* stream) {
+    if (n_tok <= 0) return TSB_OK;
+    if (!x || !parts || !wts || K < 1 || K > 32 || n % 32 != 0 || n <= 0)
+        return fail(TSB_ERR_ARG, "moe_combine: arguments");
+    const size_t sh = sizeof(float) * ((size_t) n + 256);
+    if (sh > 200 * 1024) return fail(TSB_ERR_UNSUPPORTED, "moe_combine: n %d too large", n);
+    if (sh > 48 * 1024 &&
+        cudaFuncSetAttribute(k_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sh) != cudaSuccess)
+        return cuda_status("moe_combine: shared memory");
+    k_combine<<<n_tok, 1024, sh, cs(stream)>>>(x, parts, prow, wts, K, shared, sgate, sg_stride, wn, h,
+                                               (BlockQ8_1*) hq, n, eps);
+    return cuda_status("moe_combine");
+}
+
+int tsb_rms_norm_q8_1(const float* x, const float* wn, float* h, void* hq, int n, float eps, int n_tok, void* stream) {
+    if (n_tok <= 0) return TSB_OK;
+    if (!x || n <= 0 || n % 32 != 0 || (!h && !hq)) return fail(TSB_ERR_ARG, "rms_norm_q8_1: arguments");
+    k_rms_q8_1<<<n_tok, 1024, 0, cs(stream)>>>(x, wn, h, (BlockQ8_1*) hq, n, eps);
+    return cuda_status("rms_norm_q8_1");
+}
+
+int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, int rows, void* stream) {
+    if (rows <= 0) return TSB_OK;
+    if (!x || !w || !acc || n <= 0 || n_used < 1) return fail(TSB_ERR_ARG, "moe_sum: arguments");
+    k_moe_sum<<<dim3((unsigned) ((n + 255) / 256), (unsigned) rows), 256, 0, cs(stream)>>>(x, w, acc, n, n_used);
+    return cuda_status("moe_sum");
+}
+
+int tsb_debug_row_calls(int ggml_type, const void* row, const void* x_q8_1, int64_t n, int32_t* sumi, float* val,
+                        void* stream) {
+    const int64_t rb = tsb_row_bytes(ggml_type, n);
+    if (rb <= 0 || !row || !x_q8_1 || !sumi || !val) return fail(TSB_ERR_ARG, "debug_row_calls: arguments");
+    const int calls = (int) (n / qk_of(ggml_type) * cpb_of(ggml_type));
+    auto go = [&](auto kern, int tb) {
+        const size_t sh = (size_t) tb + (size_t) rb;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sh);
+        kern<<<1, 256, sh, cs(stream)>>>((const uint8_t*) row, (const BlockQ8_1*) x_q8_1, calls, sumi, val, (int) rb);
+    };
+    switch (ggml_type) {
+        case T_IQ3_XXS: go(k_row_calls<T_IQ3_XXS>, table_bytes<T_IQ3_XXS>()); break;
+        case T_IQ3_S: go(k_row_calls<T_IQ3_S>, table_bytes<T_IQ3_S>()); break;
+        case T_Q4_0: go(k_row_calls<T_Q4_0>, 0); break;
+        case T_Q8_0: go(k_row_calls<T_Q8_0>, 0); break;
+        case T_Q4_K: go(k_row_calls<T_Q4_K>, 0); break;
+        case T_Q6_K: go(k_row_calls<T_Q6_K>, 0); break;
+        default: return fail(TSB_ERR_UNSUPPORTED, "debug_row_calls: type %d", ggml_type);
+    }
+    return cuda_status("debug_row_calls");
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+"""The engines' MoE block as a sequence of expert-layer entry points (the reference's call stacks A and C:
+src/qwen35/q36_engine.cu:2821-2925 and src/gemma4/engine.cpp:2436-2457), over device buffers owned here.
+
+Qwen decode (router_mode "softmax"): router GEMV (+ shared-gate row) -> native_router_topk -> moe_group ->
+native_expert_grouped -> shared expert (one more group) -> moe_combine (x += ..., next RMS + q8_1).
+Gemma / LFM: route_rows (softmax-scaled / sigmoid+bias) and the GELU-tanh / clamped-SwiGLU activations, moe_sum.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import (ACT_SWIGLU, Groups, Q8_1_BYTES, moe_combine, moe_group, moe_sum, native_expert_grouped,
+               native_expert_layout, native_expert_scratch_bytes, native_router_topk, route_rows, router_logits_f32)
+
+
+class MoELayer:
+    """One MoE layer's device weights and work buffers for up to max_tokens tokens.
+
+    blobs: uint8 [E, blob_bytes] (the layer's expert blobs); router: fp32 [E (+1), H]; sh_blob: uint8 [bytes] or None.
+    """
+
+    def __init__(self, cfg: dict, blobs: torch.Tensor, router: torch.Tensor, sh_blob: torch.Tensor | None = None,
+                 max_tokens: int = 16, escale=None, bias=None):
+        self.cfg = cfg
+        self.H, self.F, self.E, self.K = cfg["n_embd"], cfg["n_ff"], cfg["n_expert"], cfg["n_used"]
+        self.dev = blobs.device
+        self.blobs, self.router, self.sh_blob = blobs, router.contiguous(), sh_blob
+        self.L = native_expert_layout(cfg["gu_type"], cfg["d_type"], self.H, self.F)
+        assert blobs.shape[-1] == self.L.bytes
+        self.stride = int(blobs.stride(0)) if blobs.dim() > 1 else int(self.L.bytes)
+        self.escale, self.bias = escale, bias
+        self.max_tokens = max_tokens
+        n_ent = max_tokens * self.K
+        dev = self.dev
+        self.rows = self.router.shape[0]
+        self.logits = torch.empty((max_tokens, self.rows), dtype=torch.float32, device=dev)
+        self.ids = torch.empty((max_tokens, self.K), dtype=torch.int32, device=dev)
+        self.w = torch.empty((max_tokens, self.K), dtype=torch.float32, device=dev)
+        self.groups = Groups(n_ent, dev)
+        self.scratch = torch.empty(native_expert_scratch_bytes(n_ent, max(self.F, cfg.get("sh_n_ff") or 0)) // 4 + 64,
+                                   dtype=torch.float32, device=dev)
+        self.parts = torch.empty((n_ent, self.H), dtype=torch.float32, device=dev)
+        self.Ls = None
+        if sh_blob is not None and cfg.get("sh_n_ff"):
+            self.Ls = native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], self.H, cfg["sh_n_ff"])
+            self.shared = torch.empty((max_tokens, self.H), dtype=torch.float32, device=dev)
+            self.sh_groups = Groups(max_tokens, dev)
+            self.sh_groups.grp_ptr[0] = sh_blob.data_ptr()
+            self.sh_groups.ent_dst.copy_(torch.arange(max_tokens, dtype=torch.int32))
+            self.sh_groups.ent_tok.copy_(torch.arange(max_tokens, dtype=torch.int32))
+            self.sh_groups.n_groups.fill_(1)
+            self._sh_T = -1
+
+    def _shared_for(self, T: int):
+        if self._sh_T != T:
+            self.sh_groups.grp_start[0] = 0
+            self.sh_groups.grp_start[1] = T
+            self._sh_T = T
+
+    def forward(self, x: torch.Tensor, h: torch.Tensor, hq: torch.Tensor, h_next: torch.Tensor | None = None,
+                hq_next: torch.Tensor | None = None, eps: float = 1e-6, stream=None):
+        """x += MoE(h) for T = x.shape[0] tokens; h (fp32) feeds the router, hq (q8_1) the experts.  With h_next /
+        hq_next the next layer's RMS-normed input and its q8_1 image are written too."""
+        cfg = self.cfg
+        T = x.shape[0]
+        K, E = self.K, self.E
+        logits = self.logits[:T]
+        router_logits_f32(self.router, h, logits, ld=self.rows, stream=stream)
+        mode = cfg["router_mode"]
+        if mode == "softmax":
+            native_router_topk(logits, K, E, self.ids[:T], self.w[:T], stream=stream)
+        elif mode == "softmax_scaled":
+            ids, w = route_rows(logits[:, :E].contiguous(), K, 0, cfg.get("in_scale", 1.0), None, self.escale, True,
+                                0.0, stream=stream)
+            self.ids[:T].copy_(ids)
+            self.w[:T].copy_(w)
+        else:
+            ids, w = route_rows(logits[:, :E].contiguous(), K, 1, 1.0, self.bias, None, True, cfg.get("w_scale", 0.0),
+                                stream=stream)
+            self.ids[:T].copy_(ids)
+            self.w[:T].copy_(w)
+        moe_group(self.ids[:T], E, self.blobs, self.stride, self.groups, stream=stream)
+        n_ent = T * K
+        native_expert_grouped(self.L, self.groups, n_ent, n_ent, hq, self.scratch, self.parts, cfg["act"],
+                              cfg.get("limit", float("inf")), stream=stream)
+        shared = None
+        if self.Ls is not None:
+            self._shared_for(T)
+            native_expert_grouped(self.Ls, self.sh_groups, 1, T, hq, self.scratch, self.shared[:T],
+                                  cfg.get("sh_act", cfg["act"]), cfg.get("limit", float("inf")), stream=stream)
+            shared = self.shared[:T]
+        if mode == "softmax":
+            sg = logits[:, E:] if cfg.get("shared_gate") else None
+            moe_combine(x, self.parts, self.w[:T], K, shared, sg, self.rows, h=h_next, hq=hq_next, eps=eps,
+                        stream=stream)
+        else:
+            moe_sum(self.parts, self.w[:T], x, K, stream=stream)
+            if shared is not None:
+                x.add_(shared)
+        return x
