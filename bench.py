@@ -24,7 +24,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-N_LAYERS = 40
+N_LAYERS = 40   # --layers changes it for profiling captures only (a smaller device footprint); the bench is 40
 METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
 
 
@@ -149,7 +149,10 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--impl", default="tsb", choices=["tsb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     args = ap.parse_args()
+    global N_LAYERS
+    N_LAYERS = args.layers
     if args.impl == "reference":
         return reference_arm(args)
 

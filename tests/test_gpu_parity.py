@@ -95,7 +95,10 @@ def test_router_topk_vs_reference_and_oracle(cuda, ld):
         R = ref_or_skip()
         ri = torch.zeros_like(ids)
         rw = torch.zeros_like(w)
-        assert R.ref_native_router_topk(refgpu.ptr(lg), refgpu.ptr(ri), refgpu.ptr(rw), 256, 8, 100, refgpu.stream()) == 0
+        s = torch.cuda.Stream()   # the reference rejects the legacy default stream (native_router.cu:104)
+        with torch.cuda.stream(s):
+            assert R.ref_native_router_topk(refgpu.ptr(lg), refgpu.ptr(ri), refgpu.ptr(rw), 256, 8, 100,
+                                            refgpu.stream()) == 0
         torch.cuda.synchronize()
         assert torch.equal(ids, ri) and torch.equal(w, rw)
 
@@ -252,7 +255,8 @@ def test_combine_vs_reference_gpu_and_oracle(cuda):
     xd, pd, wd, sd, sgd = dev(x), dev(parts), dev(w), dev(shared), dev(sg)
     h = torch.empty((Tn, H), device="cuda")
     hq = torch.empty((Tn, H // 32 * 36), dtype=torch.uint8, device="cuda")
-    T.moe_combine(xd, pd, wd, K, sd, sgd[:, 256:], 257, h=h, hq=hq)
+    wn = torch.ones(H, device="cuda")   # the reference's combine computes h only with a norm weight
+    T.moe_combine(xd, pd, wd, K, sd, sgd[:, 256:], 257, wn=wn, h=h, hq=hq)
     gs = O.sigmoid(sg[:, 256])
     ref = O.combine(x, parts.reshape(Tn, K, H), w, shared, gs)
     assert np.allclose(xd.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)

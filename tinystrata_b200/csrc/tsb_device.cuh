@@ -140,13 +140,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ void report_error(unsigned* err, unsigned code) {
     if (err) atomicCAS(err, 0u, code);
 }
-constexpr uint32_t kWaitSpins = 1u << 26;   // ~ seconds of try_wait; a bulk copy from valid memory ends in microseconds
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s; a bulk copy from valid memory completes in microseconds
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned site) {
-    for (uint32_t i = 0; i < kWaitSpins; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-    report_error(err, site);
-    return false;
+        if ((i & 255u) == 0 && globaltimer() - t0 > kWaitNs) {
+            report_error(err, site);
+            return false;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------------------------------------- tables

@@ -56,20 +56,19 @@ __device__ __forceinline__ IqTab make_tab(const uint8_t* tab, int lane) {
 }
 
 // ------------------------------------------------------------------------------------------------ per-warp pipeline
-template <int STAGES>
 struct WarpRing {
     uint8_t* buf;
     uint64_t* bar;
     uint32_t stage_bytes;
     uint32_t parity;   // bit s: the parity the next wait on stage s expects
 
-    __device__ void init(uint8_t* b, uint64_t* br, uint32_t sb, int lane) {
+    __device__ void init(uint8_t* b, uint64_t* br, uint32_t sb, int nst, int lane) {
         buf = b;
         bar = br;
         stage_bytes = sb;
         parity = 0;
         if (lane == 0)
-            for (int s = 0; s < STAGES; ++s) mbar_init(&bar[s], 1);
+            for (int s = 0; s < nst; ++s) mbar_init(&bar[s], 1);
         fence_mbar_init();
         __syncwarp();
     }
@@ -157,6 +156,7 @@ __device__ __forceinline__ void row_dot_packed(const uint8_t* rows, size_t row_b
 
 // ------------------------------------------------------------------------------------------------ gate/up kernel
 struct GuParams {
+    int nst;               // stages per warp ring (1..kMaxStages)
     GroupArgs g;
     const BlockQ8_1* xq;   // [tokens][n_embd / 32]
     int n_embd, n_ff;
@@ -168,7 +168,8 @@ struct GuParams {
 };
 
 constexpr int kWarps = 8;
-constexpr int kStages = 3;
+constexpr int kMaxStages = 3;
+constexpr size_t kSmemBudget = 200 * 1024;
 
 // Task i of the call: group i / n_ff, row i % n_ff (its gate row and its up row).  Warp w of W takes tasks
 // [w n / W, (w + 1) n / W): one group for long stretches, so its activations stay in registers.
@@ -180,16 +181,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
     const uint32_t stage_bytes = (uint32_t) (2 * p.gu_row);
     uint64_t* bars = (uint64_t*) (smem + TB);
     uint8_t* stages = smem + TB + 128 * 8;
-    build_tables<TY>(smem);
-    const IqTab tab = make_tab(smem, lane);
-    WarpRing<kStages> ring;
-    ring.init(stages + (size_t) warp * kStages * stage_bytes, bars + warp * kStages, stage_bytes, lane);
+    const int nst = p.nst;
+    WarpRing ring;
+    ring.init(stages + (size_t) warp * nst * stage_bytes, bars + warp * kMaxStages, stage_bytes, nst, lane);
 
     const int ng = *p.g.n_groups;
     const long long n_tasks = (long long) ng * p.n_ff;
     const long long W = (long long) gridDim.x * kWarps, wg = (long long) blockIdx.x * kWarps + warp;
     const long long lo = n_tasks * wg / W, hi = n_tasks * (wg + 1) / W;
-    if (lo >= hi) return;
     const int C = p.n_embd / Fmt<TY>::qk * Fmt<TY>::cpb;
     const int xb = p.n_embd / 32;
 
@@ -197,17 +196,20 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
         const int g = (int) (i / p.n_ff), r = (int) (i % p.n_ff);
         a = (const uint8_t*) p.g.grp_ptr[g] + (size_t) r * p.gu_row;
     };
-    // prologue
-    for (int s = 0; s < kStages; ++s)
+    // prologue: the first stages' copies go out before the tables are built
+    for (int s = 0; s < nst; ++s)
         if (lo + s < hi) {
             const uint8_t* a;
             src_of(lo + s, a);
             ring.issue2(s, a, (uint32_t) p.gu_row, a + p.up_off, (uint32_t) p.gu_row, lane);
         }
+    build_tables<TY>(smem);
+    const IqTab tab = make_tab(smem, lane);
+    if (lo >= hi) return;
     typename Fmt<TY>::Act act[NC][J];
     int cur_g = -1, cur_e = -1;
     for (long long i = lo; i < hi; ++i) {
-        const int s = (int) ((i - lo) % kStages);
+        const int s = (int) ((i - lo) % nst);
         const int g = (int) (i / p.n_ff), r = (int) (i % p.n_ff);
         const int e0 = p.g.grp_start[g], e1 = p.g.grp_start[g + 1];
         if (!ring.wait(s, p.err, 0x100u)) return;
@@ -238,9 +240,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
                 if (c < nc && lane == c) p.h[(size_t) (eb + c) * p.n_ff + r] = act_value(p.act, sg[c], su[c], p.limit);
         }
         __syncwarp();
-        if (i + kStages < hi) {
+        if (i + nst < hi) {
             const uint8_t* a;
-            src_of(i + kStages, a);
+            src_of(i + nst, a);
             ring.issue2(s, a, (uint32_t) p.gu_row, a + p.up_off, (uint32_t) p.gu_row, lane);
         }
     }
@@ -248,6 +250,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
 
 // ------------------------------------------------------------------------------------------------ down kernel
 struct DownParams {
+    int nst;
     GroupArgs g;
     const float* h;        // [cap_entries][n_ff], quantised to q8_1 on the fly (the reference's swiglu_q8_1 step)
     int n_embd, n_ff;
@@ -267,17 +270,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_down(DownParams p) {
     const uint32_t stage_bytes = (uint32_t) (p.R * p.d_row);
     uint64_t* bars = (uint64_t*) (smem + TB);
     uint8_t* stages = smem + TB + 128 * 8;
-    build_tables<TY>(smem);
-    const IqTab tab = make_tab(smem, lane);
-    WarpRing<kStages> ring;
-    ring.init(stages + (size_t) warp * kStages * stage_bytes, bars + warp * kStages, stage_bytes, lane);
+    const int nst = p.nst;
+    WarpRing ring;
+    ring.init(stages + (size_t) warp * nst * stage_bytes, bars + warp * kMaxStages, stage_bytes, nst, lane);
 
     const int ng = *p.g.n_groups;
     const int chunks = p.n_embd / p.R;
     const long long n_tasks = (long long) ng * chunks;
     const long long W = (long long) gridDim.x * kWarps, wg = (long long) blockIdx.x * kWarps + warp;
     const long long lo = n_tasks * wg / W, hi = n_tasks * (wg + 1) / W;
-    if (lo >= hi) return;
     const int C = p.n_ff / Fmt<TY>::qk * Fmt<TY>::cpb;
     const int P = C < 32 ? 32 / C : 1;
 
@@ -285,13 +286,16 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_down(DownParams p) {
         const int g = (int) (i / chunks), ch = (int) (i % chunks);
         return (const uint8_t*) p.g.grp_ptr[g] + p.down_off + (size_t) ch * p.R * p.d_row;
     };
-    for (int s = 0; s < kStages; ++s)
+    for (int s = 0; s < nst; ++s)
         if (lo + s < hi) ring.issue2(s, src_of(lo + s), stage_bytes, nullptr, 0, lane);
+    build_tables<TY>(smem);
+    const IqTab tab = make_tab(smem, lane);
+    if (lo >= hi) return;
 
     typename Fmt<TY>::Act act[NC][J];
     int cur_g = -1, cur_e = -1;
     for (long long i = lo; i < hi; ++i) {
-        const int s = (int) ((i - lo) % kStages);
+        const int s = (int) ((i - lo) % nst);
         const int g = (int) (i / chunks), r0 = (int) (i % chunks) * p.R;
         const int e0 = p.g.grp_start[g], e1 = p.g.grp_start[g + 1];
         if (!ring.wait(s, p.err, 0x200u)) return;
@@ -336,12 +340,18 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_down(DownParams p) {
             }
         }
         __syncwarp();
-        if (i + kStages < hi) ring.issue2(s, src_of(i + kStages), stage_bytes, nullptr, 0, lane);
+        if (i + nst < hi) ring.issue2(s, src_of(i + nst), stage_bytes, nullptr, 0, lane);
     }
 }
 
-template <int TY> __host__ __device__ constexpr size_t expert_smem(uint32_t stage_bytes) {
-    return (size_t) table_bytes<TY>() + 128 * 8 + (size_t) kWarps * kStages * stage_bytes;
+// stages per warp that fit the budget beside the tables (0: the stage itself does not fit)
+template <int TY> inline int expert_stages(uint32_t stage_bytes) {
+    const size_t avail = kSmemBudget - table_bytes<TY>() - 128 * 8;
+    const size_t n = avail / ((size_t) kWarps * stage_bytes);
+    return (int) (n < (size_t) kMaxStages ? n : (size_t) kMaxStages);
+}
+template <int TY> inline size_t expert_smem(uint32_t stage_bytes, int nst) {
+    return (size_t) table_bytes<TY>() + 128 * 8 + (size_t) kWarps * nst * stage_bytes;
 }
 
 }  // namespace tsb

@@ -434,7 +434,9 @@ static int launch_gu_t(const tsb_expert_layout* L, const GroupArgs& g, int64_t c
     p.limit = limit;
     p.err = di->err;
     const uint32_t sb = (uint32_t) (2 * L->gu_row);
-    const size_t smem = expert_smem<TY>(sb);
+    p.nst = expert_stages<TY>(sb);
+    if (p.nst < 1) return fail(TSB_ERR_UNSUPPORTED, "expert gate/up: a %u-byte row pair does not fit", sb);
+    const size_t smem = expert_smem<TY>(sb, p.nst);
     auto kern = k_expert_gu<TY, J, 4>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
         return cuda_status("expert gate/up: shared memory");
@@ -464,7 +466,9 @@ static int launch_down_t(const tsb_expert_layout* L, const GroupArgs& g, int64_t
     p.out = out;
     p.err = di->err;
     const uint32_t sb = (uint32_t) (R * L->d_row);
-    const size_t smem = expert_smem<TY>(sb);
+    p.nst = expert_stages<TY>(sb);
+    if (p.nst < 1) return fail(TSB_ERR_UNSUPPORTED, "expert down: a %u-byte chunk does not fit", sb);
+    const size_t smem = expert_smem<TY>(sb, p.nst);
     auto kern = k_expert_down<TY, J, 4>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
         return cuda_status("expert down: shared memory");
@@ -585,9 +589,9 @@ uint64_t tsb_native_expert_scratch_bytes(int64_t cap_entries, int64_t n_ff) {
 }
 
 int tsb_quantize_q8_1_rows(const float* x, int64_t n_rows, int64_t n_cols, void* y, void* stream) {
+    if (n_rows == 0) return TSB_OK;
     if (!x || !y || n_rows < 0 || n_cols % 32 != 0) return fail(TSB_ERR_ARG, "quantize_q8_1_rows: arguments");
     const long long n = n_rows * n_cols;
-    if (n == 0) return TSB_OK;
     k_quantize_q8_1<<<(unsigned) ((n + 255) / 256), 256, 0, cs(stream)>>>(x, (BlockQ8_1*) y, n);
     return cuda_status("quantize_q8_1_rows");
 }
