@@ -150,6 +150,7 @@ def main():
     ap.add_argument("--impl", default="tsb", choices=["tsb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
+    ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
     args = ap.parse_args()
     global N_LAYERS
     N_LAYERS = args.layers
@@ -184,55 +185,82 @@ def main():
     out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
 
     stream = torch.cuda.Stream(device)
+    D = TS.DecodeStack(cfg, st["blobs"], st["routers"], st["sh_blobs"], n_tok=T)
+    torch.cuda.synchronize()
 
-    def step_body():
+    # verification pass (eager, untimed): the fused step against the layer-by-layer entry points, routing taken
+    with torch.cuda.stream(stream):
+        x.copy_(x0_dev)
         TS.rms_norm_q8_1(x, h, hq, stream=stream)
         for M in layers:
             M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream)
-
-    # verification pass (eager, untimed): routing actually taken, and finite outputs
-    with torch.cuda.stream(stream):
+        x_layerwise = x.clone()
         x.copy_(x0_dev)
-        step_body()
+        D.forward(x, stream=stream)
     stream.synchronize()
-    assert TS.device_error() == 0
+    assert D.error() == 0 and TS.device_error() == 0
     assert torch.isfinite(x).all(), "non-finite layer output"
-    distinct = [int(torch.unique(M.ids[:T]).numel()) for M in layers]
+    rel = float(((x - x_layerwise).abs().max() / x_layerwise.pow(2).mean().sqrt()).item())
+    same_routing = all(torch.equal(D.ids[l], M.ids[:T]) for l, M in enumerate(layers))
+    distinct = [int(torch.unique(D.ids[l]).numel()) for l in range(N_LAYERS)]
     L, Ls = layers[0].L, layers[0].Ls
     bytes_layer = [d * L.bytes + Ls.bytes + (E + 1) * H * 4 for d in distinct]
     alg_bytes_per_layer = float(np.mean(bytes_layer))
 
-    # capture one step as a graph
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        x.copy_(x0_dev)
-        with torch.cuda.graph(graph, stream=stream):
-            step_body()
-    launches_per_step = 1 + N_LAYERS * 8   # rms; per layer: logits, top-k, group, gu, down, shared gu, shared down, combine
-
-    def replay(n):
-        for _ in range(n):
-            graph.replay()
-
-    # device-timed region (inputs resident)
-    with torch.cuda.stream(stream):
-        x.copy_(x0_dev)
-        replay(max(3, args.warmup))
-    stream.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
+    if args.trace:
         with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(args.steps):
-                x.copy_(x0_dev)
-                graph.replay()
-            ev1.record(stream)
+            x.copy_(x0_dev)
         stream.synchronize()
+        tr = D.trace(x, stream=stream).double()
+        names = ["start", "P0", "P1", "bar1", "route", "P2", "bar2", "P3", "bar3", "pr:P1", "pr:route", "pr:P2",
+                 "pr:P3"]
+        rows = []
+        for l in range(1, N_LAYERS):
+            t0 = tr[l, 0].min()
+            rows.append([((tr[l, e] - t0) / 1e3).mean().item() for e in range(13)] +
+                        [((tr[l, e] - t0) / 1e3).max().item() for e in range(13)])
+        m = np.array(rows).mean(0)
+        print("phase (us from layer start): " + "  ".join(f"{n}={m[i]:.2f}/{m[13 + i]:.2f}" for i, n in
+                                                        enumerate(names)), file=sys.stderr, flush=True)
+
+    def fused_step():
+        x.copy_(x0_dev)
+        D.forward(x, stream=stream)
+
+    def layerwise_step():
+        x.copy_(x0_dev)
+        TS.rms_norm_q8_1(x, h, hq, stream=stream)
+        for M in layers:
+            M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream)
+
+    graphs = {}
+    for name, fn in (("fused", fused_step), ("layerwise", layerwise_step)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                fn()
+        graphs[name] = g
+    stream.synchronize()
+
+    def timed(g, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n):
+                g.replay()
+            e1.record(stream)
+        stream.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    # warm-up, then the device-timed region (inputs resident, 12.3 GB of weights >> L2)
+    timed(graphs["fused"], max(3, args.warmup))
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ms = timed(graphs["fused"], args.steps)
     torch.cuda.synchronize()
     barrier()
-    ms = ev0.elapsed_time(ev1) / args.steps
+    assert D.error() == 0
     if ws > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -240,14 +268,14 @@ def main():
     us_layer = ms * 1e3 / N_LAYERS
     value = ws * T / (us_layer * 1e-6)
 
-    # end to end: host input -> device, the 40 layers, device -> host, every step
+    # end to end: host input -> device, the fused step, device -> host, every step
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
             x.copy_(x0_host, non_blocking=True)
-            graph.replay()
+            D.forward(x, stream=stream)
             out_host.copy_(x, non_blocking=True)
         e1.record(stream)
     stream.synchronize()
@@ -259,26 +287,24 @@ def main():
         ms_e2e = float(t.item())
     e2e_value = ws * T / (ms_e2e * 1e3 / N_LAYERS * 1e-6)
 
-    # the dominant kernel alone: the routed gate/up GEMV of each layer, CUDA events on its stream (cold: 40 layers
-    # of distinct weights between launches of the same layer)
-    TS.native_expert_set_phase(1)
-    gu_ms = []
+    # the dominant (and only) kernel alone, CUDA events on its stream: k_decode_layers over the 40 layers
+    kms = []
     with torch.cuda.stream(stream):
-        for rep in range(3):
-            for M in layers:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                TS.native_expert_grouped(M.L, M.groups, T * K, T * K, hq, M.scratch, M.parts, stream=stream)
-                b.record(stream)
-                gu_ms.append((a, b))
+        for rep in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            x.copy_(x0_dev)
+            a.record(stream)
+            D.forward(x, stream=stream)
+            b.record(stream)
+            kms.append((a, b))
     stream.synchronize()
-    TS.native_expert_set_phase(0)
-    gu_avg_ms = float(np.mean([a.elapsed_time(b) for a, b in gu_ms[len(layers):]]))
-    gu_bytes = float(np.mean([d * L.up_off * 2 for d in distinct]))
+    k_avg_ms = float(np.mean([a.elapsed_time(b) for a, b in kms[1:]]))
+    k_bytes = float(np.sum(bytes_layer))
     peak, peak_kind = peaks()
-    gu_gbs = gu_bytes / (gu_avg_ms * 1e-3) / 1e9
-    layer_gbs = alg_bytes_per_layer / (us_layer * 1e-6) / 1e9
-
+    k_gbs = k_bytes / (k_avg_ms * 1e-3) / 1e9
+    layerwise_us = timed(graphs["layerwise"], max(3, args.steps // 2)) * 1e3 / N_LAYERS
+    gpu_launches = args.steps   # one k_decode_layers per step
+    gu_avg_ms = k_avg_ms
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
@@ -300,20 +326,21 @@ def main():
                        "distinct_experts_per_layer": float(np.mean(distinct)),
                        "l2": "inputs larger than L2 (12.3 GB of expert weights, 40 distinct layers per step)"},
             "us_per_layer": us_layer,
-            "layer_hbm_gbs": layer_gbs,
-            "roofline": {"bound": "hbm", "kernel": "k_expert_gu (routed gate/up + SwiGLU)", "achieved": gu_gbs,
-                         "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak, "peak_kind": peak_kind,
-                         "traffic": None, "algorithmic_bytes_per_launch": gu_bytes,
-                         "avg_launch_ms": gu_avg_ms,
-                         "layer_frac": layer_gbs / peak, "layer_algorithmic_bytes": alg_bytes_per_layer},
+            "layer_hbm_gbs": alg_bytes_per_layer / (us_layer * 1e-6) / 1e9,
+            "layerwise_us_per_layer": layerwise_us,
+            "fused_vs_layerwise": {"max_abs_over_rms": rel, "same_routing": same_routing},
+            "roofline": {"bound": "hbm", "kernel": "k_decode_layers (fused decode step, 40 layers)",
+                         "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
+                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": k_bytes,
+                         "avg_launch_ms": k_avg_ms, "layer_algorithmic_bytes": alg_bytes_per_layer},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": gpu_launches,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graphs
     if ws > 1:
         dist.destroy_process_group()
     return 0

@@ -125,6 +125,43 @@ int tsb_rms_norm_q8_1(const float* x, const float* wn, float* h, void* hq, int n
 /* acc[t] += sum_k w[t,k] x[t*K+k], n values per row.  Replaces moe_sum (src/gemma4/kernels.cu:358-366). */
 int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, int rows, void* stream);
 
+/* --------------------------------------------------------------------------------------------- fused decode */
+/* One layer of the fused decode path: device pointers to its expert blobs ([n_expert][blob bytes], the
+ * NativeExpertLayout of each), its fp32 router ([n_expert + 1][n_embd]: the expert rows, then the shared-expert gate
+ * row, as q36_engine.cu:1139-1142 appends it) and its shared expert blob. */
+typedef struct tsb_decode_layer {
+    const void* blobs;
+    const float* router;
+    const void* sh_blob;
+} tsb_decode_layer;
+
+typedef struct tsb_decode_desc {
+    uint32_t struct_size;            /* sizeof(tsb_decode_desc) */
+    int32_t n_layers, n_tok;         /* layers of the step; tokens (1..16) */
+    int32_t n_embd, n_ff, n_expert, n_used, sh_n_ff;
+    int32_t gu_type, d_type, sh_gu_type, sh_d_type;
+    float eps;                       /* the RMS epsilon of the layer input's norm */
+} tsb_decode_desc;
+
+/* Workspace bytes tsb_moe_decode_layers needs for this description. */
+uint64_t tsb_moe_decode_workspace_bytes(const tsb_decode_desc* d);
+/* Every layer's MoE block for n_tok decode tokens in one persistent launch (one CTA per SM, cooperative):
+ * per layer h = rms(x), router GEMV, softmax top-k, grouping, routed and shared experts, and x += the gated combine
+ * (q36_engine.cu:2821-2925 with k_moe_out_small, per layer).  x: [n_tok][n_embd] fp32, in / out.  layers: a DEVICE
+ * array of n_layers tsb_decode_layer.  ids_rec / w_rec (optional, [n_layers][n_tok][n_used]) record the routing.
+ * Supported: IQ3_XXS routed experts (n_ff 512), 256 experts, Q8_0 shared expert, SwiGLU.  Replaces the per-layer
+ * sequence f32mm + route_group + native_expert_grouped + shared expert + moe_end of the Qwen3.6 engine. */
+int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* layers, float* x, int32_t* ids_rec,
+                          float* w_rec, void* workspace, uint64_t ws_bytes, void* stream);
+/* The decode kernel's error word in `workspace` (non-zero: a bounded wait gave up).  Synchronous read. */
+int tsb_moe_decode_error(const tsb_decode_desc* d, const void* workspace, unsigned* code);
+/* The calling thread's last decode-path error message. */
+const char* tsb_decode_last_error(void);
+/* Profiling: launches made after this call stamp %globaltimer (ns) into `buf` (device, [n_layers][16][n_CTAs]
+ * u64) at each phase boundary of every layer (consumer stamps 0-8, producer stamps 9-12, see tsb_decode.cuh); null
+ * turns it off.  Process-wide; a captured graph keeps the buffer it was captured with. */
+int tsb_moe_decode_set_trace(unsigned long long* buf);
+
 /* --------------------------------------------------------------------------------------------- test hook */
 /* The per-call integer sums and float values of one weight row (n values) against one q8_1 activation, as the
  * expert kernels compute them (calls in row_dot order, src/kernels/cuda/iq_kernels.cu:695-705).  Parity tests only. */

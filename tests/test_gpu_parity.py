@@ -268,11 +268,17 @@ def test_combine_vs_reference_gpu_and_oracle(cuda):
         h2 = torch.empty_like(h)
         hq2 = torch.empty_like(hq)
         R.ref_moe_out_small(refgpu.ptr(x2), refgpu.ptr(pd), None, refgpu.ptr(wd), K, refgpu.ptr(sd),
-                            C_ptr(sgd, 256), 257, None, refgpu.ptr(h2), H, 1e-6, refgpu.ptr(hq2), Tn, refgpu.stream())
+                            C_ptr(sgd, 256), 257, refgpu.ptr(wn), refgpu.ptr(h2), H, 1e-6, refgpu.ptr(hq2), Tn,
+                            refgpu.stream())
         torch.cuda.synchronize()
         assert np.allclose(x2.cpu().numpy(), xd.cpu().numpy(), rtol=1e-6, atol=1e-6)
+        assert np.allclose(h2.cpu().numpy(), h.cpu().numpy(), rtol=1e-6, atol=1e-6)
+        # the reference's h through the quantiser pinned bitwise to the reference's own gives this combine's hq
+        assert torch.equal(T.quantize_q8_1_rows(h2), hq) or not torch.equal(h2, h)
         bad_ds, bad_codes, maxd = O.q8_1_compare(hq.cpu().numpy(), hq2.cpu().numpy())
-        assert maxd <= 1
+        assert maxd <= 1 and bad_codes <= 8
+    bad_ds, bad_codes, maxd = O.q8_1_compare(hq.cpu().numpy(), hqr)
+    assert maxd <= 1 and bad_codes <= 8
 
 
 def C_ptr(t, offset_elems):

@@ -23,6 +23,18 @@ class TsbError(RuntimeError):
     pass
 
 
+class DecodeLayer(C.Structure):
+    """tsb_decode_layer: device pointers of one layer for the fused decode path."""
+    _fields_ = [("blobs", C.c_void_p), ("router", C.c_void_p), ("sh_blob", C.c_void_p)]
+
+
+class DecodeDesc(C.Structure):
+    _fields_ = [("struct_size", C.c_uint32), ("n_layers", C.c_int32), ("n_tok", C.c_int32), ("n_embd", C.c_int32),
+                ("n_ff", C.c_int32), ("n_expert", C.c_int32), ("n_used", C.c_int32), ("sh_n_ff", C.c_int32),
+                ("gu_type", C.c_int32), ("d_type", C.c_int32), ("sh_gu_type", C.c_int32), ("sh_d_type", C.c_int32),
+                ("eps", C.c_float)]
+
+
 class ExpertLayout(C.Structure):
     """tsb_expert_layout (the reference's NativeExpertLayout, iq_kernels.hpp:45-53)."""
     _fields_ = [("gu_type", C.c_int32), ("d_type", C.c_int32), ("n_embd", C.c_int64), ("n_ff", C.c_int64),
@@ -58,6 +70,11 @@ SIGNATURES = {
     "tsb_rms_norm_q8_1": (C.c_int, [_p, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
     "tsb_native_expert_set_phase": (C.c_int, [C.c_int]),
     "tsb_debug_row_calls": (C.c_int, [C.c_int, _p, _p, _i64, _p, _p, _p]),
+    "tsb_moe_decode_workspace_bytes": (_u64, [C.POINTER(DecodeDesc)]),
+    "tsb_moe_decode_layers": (C.c_int, [C.POINTER(DecodeDesc), _p, _p, _p, _p, _p, _u64, _p]),
+    "tsb_moe_decode_error": (C.c_int, [C.POINTER(DecodeDesc), _p, C.POINTER(C.c_uint)]),
+    "tsb_decode_last_error": (C.c_char_p, []),
+    "tsb_moe_decode_set_trace": (C.c_int, [_p]),
 }
 
 
@@ -243,6 +260,56 @@ def device_error(clear: bool = True) -> int:
     code = C.c_uint(0)
     _check(lib().tsb_device_error(C.byref(code), int(clear)), "device_error")
     return int(code.value)
+
+
+class DecodeStack:
+    """The fused decode path over n_layers resident layers: one persistent launch per step
+    (tsb_moe_decode_layers).  blobs [L][E][bytes] uint8, routers [L][E + 1][H] fp32, sh_blobs [L][bytes] uint8."""
+
+    def __init__(self, cfg: dict, blobs, routers, sh_blobs, n_tok: int, eps: float = 1e-6, record: bool = True):
+        import torch
+        self.cfg = cfg
+        L = blobs.shape[0]
+        self.desc = DecodeDesc(C.sizeof(DecodeDesc), L, n_tok, cfg["n_embd"], cfg["n_ff"], cfg["n_expert"],
+                               cfg["n_used"], cfg["sh_n_ff"], cfg["gu_type"], cfg["d_type"], cfg["sh_gu_type"],
+                               cfg["sh_d_type"], eps)
+        dev = blobs.device
+        tab = torch.tensor([[blobs[l].data_ptr(), routers[l].data_ptr(), sh_blobs[l].data_ptr()] for l in range(L)],
+                           dtype=torch.int64)
+        self.layers = tab.to(dev)
+        self.ws_bytes = int(lib().tsb_moe_decode_workspace_bytes(C.byref(self.desc)))
+        self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
+        K = cfg["n_used"]
+        self.ids = torch.zeros((L, n_tok, K), dtype=torch.int32, device=dev) if record else None
+        self.w = torch.zeros((L, n_tok, K), dtype=torch.float32, device=dev) if record else None
+        self._keep = (blobs, routers, sh_blobs)
+
+    def forward(self, x, stream=None):
+        rc = lib().tsb_moe_decode_layers(C.byref(self.desc), _ptr(self.layers), _ptr(x), _ptr(self.ids), _ptr(self.w),
+                                         _ptr(self.ws), self.ws_bytes, _stream(stream))
+        if rc != 0:
+            raise TsbError(f"moe_decode_layers: status {rc}: {lib().tsb_decode_last_error().decode()}")
+        return x
+
+    def trace(self, x, stream=None):
+        """One traced step: per layer, per phase the mean / max over CTAs of the stamp offsets (us from the launch's
+        first stamp).  Returns (stamps [L][16][CTAs] int64 tensor, summary dict)."""
+        import torch
+        L = self.desc.n_layers
+        sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+        buf = torch.zeros((L, 16, sms), dtype=torch.int64, device=x.device)
+        _check(lib().tsb_moe_decode_set_trace(_ptr(buf)), "set_trace")
+        try:
+            self.forward(x, stream)
+            torch.cuda.synchronize()
+        finally:
+            lib().tsb_moe_decode_set_trace(None)
+        return buf.cpu()
+
+    def error(self) -> int:
+        code = C.c_uint(0)
+        _check(lib().tsb_moe_decode_error(C.byref(self.desc), _ptr(self.ws), C.byref(code)), "moe_decode_error")
+        return int(code.value)
 
 
 from .layer import MoELayer  # noqa: E402  (host mirror of the engines' MoE block)

@@ -58,6 +58,26 @@ __device__ __forceinline__ QB qb_from_f32(const float* x32) {
     return r;
 }
 
+// The same from memory other CTAs of the running kernel write (L1 bypassed).
+__device__ __forceinline__ QB qb_from_f32_cg(const float* x32) {
+    float v[32];
+    const float4* p = (const float4*) x32;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = __ldcg(p + i);
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
+    }
+    const Q8Block b = q8_1_lane(v);
+    QB r;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r.q[i] = b.q[i];
+    r.d = __low2float(b.ds);
+    return r;
+}
+
 template <int TY> struct Fmt;
 
 // ------------------------------------------------------------------------------------------------ IQ3_XXS (type 18)

@@ -24,17 +24,18 @@ template <int TY> __host__ __device__ constexpr int table_bytes() {
     return TY == T_IQ3_XXS ? kIqTabBytes : TY == T_IQ3_S ? kIqTabBytes + 2048 : 0;
 }
 
-// Fill the lane-banked IQ3_XXS grid and sign masks (and the plain IQ3_S grid when asked); whole CTA, then sync.
+// Fill the lane-banked IQ3_XXS grid and sign masks (and the plain IQ3_S grid when asked) with threads
+// [0, nthreads); the caller synchronises them afterwards.
 template <int TY>
-__device__ void build_tables(uint8_t* tab) {
+__device__ void fill_tables(uint8_t* tab, int nthreads) {
     if constexpr (TY == T_IQ3_XXS) {
         // grid: 256 indices x 32 lanes; sign masks: 128 indices x 16 lane slots x 8 bytes
-        for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) {
+        for (int i = threadIdx.x; i < 256 * 8; i += nthreads) {
             const int idx = i >> 3, q = i & 7;
             const uint32_t g = g_iq3xxs_grid[idx];
             *(uint4*) (tab + idx * 256 + q * 16) = make_uint4(g, g, g, g);
         }
-        for (int i = threadIdx.x; i < 128 * 8; i += blockDim.x) {
+        for (int i = threadIdx.x; i < 128 * 8; i += nthreads) {
             const int s = i >> 3, q = i & 7;
             const uint32_t ks = g_ksigns[s];
             const uint32_t m0 = spread4(ks & 15u), m1 = spread4(ks >> 4);
@@ -42,8 +43,13 @@ __device__ void build_tables(uint8_t* tab) {
         }
     } else if constexpr (TY == T_IQ3_S) {
         uint32_t* g3 = (uint32_t*) (tab + kIqTabBytes);
-        for (int i = threadIdx.x; i < 512; i += blockDim.x) g3[i] = g_iq3s_grid[i];
+        for (int i = threadIdx.x; i < 512; i += nthreads) g3[i] = g_iq3s_grid[i];
     }
+}
+// Whole CTA, then __syncthreads.
+template <int TY>
+__device__ void build_tables(uint8_t* tab) {
+    fill_tables<TY>(tab, blockDim.x);
     __syncthreads();
 }
 
