@@ -153,7 +153,10 @@ uint64_t tsb_moe_decode_workspace_bytes(const tsb_decode_desc* d);
  * sequence f32mm + route_group + native_expert_grouped + shared expert + moe_end of the Qwen3.6 engine. */
 int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* layers, float* x, int32_t* ids_rec,
                           float* w_rec, void* workspace, uint64_t ws_bytes, void* stream);
-/* The decode kernel's error word in `workspace` (non-zero: a bounded wait gave up).  Synchronous read. */
+/* The decode kernel's error record in `workspace`: code[0] non-zero when a bounded wait gave up (its site), code[1..4]
+ * that wait's context (unit sequence and layer, producer progress, claim counter, CTA, raw barrier words).  `code`
+ * holds 128 words.
+ * Synchronous read. */
 int tsb_moe_decode_error(const tsb_decode_desc* d, const void* workspace, unsigned* code);
 /* The calling thread's last decode-path error message. */
 const char* tsb_decode_last_error(void);

@@ -48,7 +48,8 @@ def test_fused_decode_matches_layerwise(cuda, stack, Tn):
     x2 = x0.clone()
     D.forward(x2)
     torch.cuda.synchronize()
-    assert D.error() == 0 and T.device_error() == 0
+    assert D.error() == 0, " ".join(str(v) for v in D.error_detail)
+    assert T.device_error() == 0
     for l in range(3):
         assert torch.equal(D.ids[l], ids_ref[l]), f"layer {l} routing"
     err, cos = tol(x2.cpu().numpy(), x1.cpu().numpy())

@@ -72,7 +72,7 @@ SIGNATURES = {
     "tsb_debug_row_calls": (C.c_int, [C.c_int, _p, _p, _i64, _p, _p, _p]),
     "tsb_moe_decode_workspace_bytes": (_u64, [C.POINTER(DecodeDesc)]),
     "tsb_moe_decode_layers": (C.c_int, [C.POINTER(DecodeDesc), _p, _p, _p, _p, _p, _u64, _p]),
-    "tsb_moe_decode_error": (C.c_int, [C.POINTER(DecodeDesc), _p, C.POINTER(C.c_uint)]),
+    "tsb_moe_decode_error": (C.c_int, [C.POINTER(DecodeDesc), _p, _p]),
     "tsb_decode_last_error": (C.c_char_p, []),
     "tsb_moe_decode_set_trace": (C.c_int, [_p]),
 }
@@ -307,9 +307,18 @@ class DecodeStack:
         return buf.cpu()
 
     def error(self) -> int:
-        code = C.c_uint(0)
-        _check(lib().tsb_moe_decode_error(C.byref(self.desc), _ptr(self.ws), C.byref(code)), "moe_decode_error")
-        return int(code.value)
+        code = (C.c_uint * 128)()
+        _check(lib().tsb_moe_decode_error(C.byref(self.desc), _ptr(self.ws), code), "moe_decode_error")
+        self.error_detail = [hex(int(c)) for c in code[:106]] + ["layout"] + [hex(int(c)) for c in code[110:117]]
+        if code[0]:
+            import torch
+            w = self.ws.view(torch.int32)
+            # progress words after the error record: (layer << 8) | phase stamp of each CTA
+            off = (self.ws_bytes - 8192) // 4 + 128
+            prog = w[off:off + torch.cuda.get_device_properties(self.ws.device).multi_processor_count].cpu().tolist()
+            from collections import Counter
+            self.error_detail.append(sorted(Counter(hex(v) for v in prog).items()))
+        return int(code[0])
 
 
 from .layer import MoELayer  # noqa: E402  (host mirror of the engines' MoE block)

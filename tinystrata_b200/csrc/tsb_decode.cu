@@ -31,7 +31,7 @@ WsLayout ws_layout(const tsb_decode_desc* d) {
     w.hbuf = o;   o += al((size_t) d->n_tok * d->n_used * d->n_ff * 4);
     w.sh_out = o; o += al((size_t) d->n_tok * d->n_embd * 4);
     w.bar = o;    o += 256;
-    w.err = o;    o += 256;
+    w.err = o;    o += 8192;   // error word, its context (words 1..127), one progress word per CTA from word 128
     w.total = o;
     return w;
 }
@@ -68,8 +68,13 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     if (p.gu_row % 16 || p.sgu_row % 16 || p.sd_row % 16 || p.blob_bytes % 16 || p.rt_per_unit < 1 ||
         2 * p.sgu_row > kSlotBytes || p.dn_per_unit < 1 || H % p.R)
         return dfail(TSB_ERR_UNSUPPORTED, "decode: rows do not fit the ring slots");
-    smem = (size_t) kIqTabBytes + (size_t) kSlots * kSlotBytes + sizeof(DecShared) + 128 + (size_t) T * H +
-           (size_t) T * (H / 32) * 4 + (size_t) kDecMaxEnt * kDecMaxRows * 4;
+    int dev = 0, reserved = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    p.smem_base = (uint32_t) reserved;
+    if (p.smem_base + (uint32_t) kSlots * kSlotBytes > 0x10000u)
+        return dfail(TSB_ERR_UNSUPPORTED, "decode: %d reserved bytes leave no room for the ring", reserved);
+    smem = dec_smem(p.smem_base, T, H, F, FS, K).total;
     return TSB_OK;
 }
 
@@ -120,7 +125,7 @@ int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* laye
     auto kern = k_decode_layers<8>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
         return dfail(TSB_ERR_CUDA, "decode: shared memory attribute: %s", cudaGetErrorString(cudaGetLastError()));
-    if (cudaMemsetAsync(ws + w.bar, 0, 512, s) != cudaSuccess)
+    if (cudaMemsetAsync(ws + w.bar, 0, w.total - w.bar, s) != cudaSuccess)
         return dfail(TSB_ERR_CUDA, "decode: memset: %s", cudaGetErrorString(cudaGetLastError()));
     void* args[] = {&p};
     const cudaError_t e = cudaLaunchCooperativeKernel((const void*) kern, dim3(sms), dim3(kDecThreads), args, smem, s);
@@ -131,7 +136,7 @@ int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* laye
 int tsb_moe_decode_error(const tsb_decode_desc* d, const void* workspace, unsigned* code) {
     if (!d || !workspace || !code) return dfail(TSB_ERR_ARG, "decode_error: null argument");
     const WsLayout w = ws_layout(d);
-    if (cudaMemcpy(code, (const uint8_t*) workspace + w.err, sizeof(unsigned), cudaMemcpyDeviceToHost) != cudaSuccess)
+    if (cudaMemcpy(code, (const uint8_t*) workspace + w.err, sizeof(unsigned) * 128, cudaMemcpyDeviceToHost) != cudaSuccess)
         return dfail(TSB_ERR_CUDA, "decode_error: %s", cudaGetErrorString(cudaGetLastError()));
     return TSB_OK;
 }

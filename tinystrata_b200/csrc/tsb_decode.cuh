@@ -26,7 +26,7 @@
 namespace tsb {
 
 constexpr int kDecWarps = 16, kDecConsumers = 15, kDecThreads = kDecWarps * 32, kDecCThreads = kDecConsumers * 32;
-constexpr int kSlots = 24;
+constexpr int kSlots = 14;   // 14 x 4352 bytes below the tables (which sit at shared address 0x10000)
 constexpr uint32_t kSlotBytes = 4352;
 constexpr int kDecMaxT = 16, kDecMaxEnt = 128, kDecMaxRows = 16;   // rows of H per CTA in P3 (<= 4 chunks of 4)
 
@@ -54,6 +54,7 @@ struct DecParams {
     unsigned* err;
     unsigned long long* trace;   // optional phase stamps: [layer][kTraceEvents][CTA] of %globaltimer, or null
     float eps;
+    uint32_t smem_base;       // the shared-window address the dynamic shared memory starts at (checked)
 };
 constexpr int kTraceEvents = 16;
 
@@ -61,6 +62,14 @@ struct DecShared {
     uint64_t full[kSlots], empty[kSlots], route;
     int claim;
     int abort;
+    volatile int prod_seq, prod_state;   // the producer's progress (diagnostics of a wait that gives up)
+    volatile int warp_unit[kDecConsumers];   // the ring sequence each consumer warp waits on or works on
+    volatile int warp_state[kDecConsumers];  // 1 waiting, 2 computing, 3 released
+    // The ring lap the producer has started on each slot.  A consumer may claim a unit a whole lap ahead of a slot's
+    // previous unit; waiting on the full barrier's parity is only unambiguous once the producer has started that lap
+    // (a barrier still in phase lap - 1 answers a wait on parity lap & 1 as complete: the preceding phase).
+    volatile int slot_lap[kSlots];
+    unsigned canary;
     int n_groups;
     float rms[kDecMaxT];
     float gs[kDecMaxT];
@@ -70,11 +79,49 @@ struct DecShared {
     float red[256];
 };
 
+// Offsets inside the dynamic shared memory (dynamic base at shared address b0 <= 0x10000 - kSlots * kSlotBytes):
+//   [0, kSlots * kSlotBytes)              the ring
+//   [0x10000 - b0, +64 KB)                the IQ3_XXS tables at shared address 0x10000
+//   [0x20000 - b0, ...)                   DecShared, parts [kDecMaxEnt][kDecMaxRows], then the activation union:
+//       P0..P2: xq codes [T][H], xq scales [T][H / 32], hshq codes [T][FS], hshq scales [T][FS / 32]
+//       P3:     hq codes [T K][F], hq scales [T K][F / 32]
+struct DecSmem {
+    uint32_t tab, shared, parts, uni, xq_d, hs, hs_d, hq_d, total;
+};
+__host__ __device__ inline DecSmem dec_smem(uint32_t b0, int T, int H, int F, int FS, int K) {
+    auto al = [](uint32_t v, uint32_t a) { return (v + a - 1) / a * a; };
+    DecSmem m;
+    m.tab = 0x10000u - b0;
+    m.shared = 0x20000u - b0;
+    m.parts = al(m.shared + (uint32_t) sizeof(DecShared), 16);
+    m.uni = al(m.parts + (uint32_t) (kDecMaxEnt * kDecMaxRows * 4), 128);
+    m.xq_d = m.uni + (uint32_t) (T * H);
+    m.hs = al(m.xq_d + (uint32_t) (T * (H / 32) * 4), 16);
+    m.hs_d = m.hs + (uint32_t) (T * FS);
+    const uint32_t end1 = m.hs_d + (uint32_t) (T * (FS / 32) * 4);
+    m.hq_d = m.uni + (uint32_t) (T * K * F);
+    const uint32_t end2 = m.hq_d + (uint32_t) (T * K * (F / 32) * 4);
+    m.total = end1 > end2 ? end1 : end2;
+    return m;
+}
+
 // -------------------------------------------------------------------------------------------------- small helpers
+// A wait that gave up: the first one records its site and four words of context after the error word.
+__device__ __forceinline__ void report_detail(unsigned* err, unsigned site, unsigned a, unsigned b, unsigned c,
+                                              unsigned d) {
+    if (err && atomicCAS(err, 0u, site) == 0u) {
+        err[1] = a;
+        err[2] = b;
+        err[3] = c;
+        err[4] = d;
+        __threadfence();
+    }
+}
 // Phase stamps (consumers: 0 layer start, 1 P0, 2 P1, 3 barrier, 4 routing, 5 P2, 6 barrier, 7 P3 + combine,
 // 8 barrier; producer: 9 P1 issued, 10 routing seen, 11 P2 issued, 12 P3 issued).
 __device__ __forceinline__ void stamp(const DecParams& p, int l, int ev) {
     if (p.trace) p.trace[((size_t) l * kTraceEvents + ev) * gridDim.x + blockIdx.x] = globaltimer();
+    if (ev < 9) ((volatile unsigned*) p.err)[128 + blockIdx.x] = ((unsigned) l << 8) | (unsigned) ev;
 }
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -94,9 +141,17 @@ __device__ bool grid_barrier(const DecParams& p, DecShared& S, unsigned& target,
         __threadfence();
         atomicAdd(p.bar, 1u);
         const uint64_t t0 = globaltimer();
-        while (ld_acquire(p.bar) < target) {
+        unsigned v;
+        while ((v = ld_acquire(p.bar)) < target) {
             if (globaltimer() - t0 > kWaitNs || S.abort) {
                 report_error(p.err, site);
+                if (p.err && atomicCAS(p.err + 99, 0u, 1u) == 0u) {
+                    p.err[100] = site;
+                    p.err[101] = v;
+                    p.err[102] = target;
+                    p.err[103] = (unsigned) S.prod_state;
+                    p.err[104] = blockIdx.x;
+                }
                 S.abort = 1;
                 break;
             }
@@ -138,7 +193,7 @@ struct Producer {
                 const uint64_t t0 = globaltimer();
                 while (!mbar_try_wait(&S->empty[slot], par)) {
                     if (globaltimer() - t0 > kWaitNs || S->abort) {
-                        report_error(p->err, 0x310u);
+                        report_detail(p->err, 0x310u, seq, (unsigned) S->prod_state, (unsigned) S->claim, blockIdx.x);
                         S->abort = 1;
                         return false;
                     }
@@ -148,7 +203,16 @@ struct Producer {
         return true;
     }
     __device__ uint8_t* slot_ptr(uint32_t slot) const { return ring + (size_t) slot * kSlotBytes; }
-    __device__ void finish(uint32_t slot) { ++seq; (void) slot; }
+    // this unit's lap on its slot, published for the consumers (before its bytes are expected)
+    __device__ void start(uint32_t slot) {
+        S->slot_lap[slot] = (int) (seq / kSlots);
+        __threadfence_block();
+    }
+    __device__ void finish(uint32_t slot) {
+        ++seq;
+        S->prod_seq = (int) seq;
+        (void) slot;
+    }
 };
 
 // -------------------------------------------------------------------------------------------------- activations
@@ -156,7 +220,7 @@ struct Producer {
 struct XqView {
     const int8_t* codes;
     const float* d;
-    int H;
+    int H;   // values per row
     __device__ QB block(int t, int b) const {
         QB r;
         const int4* c = (const int4*) (codes + (size_t) t * H + 32 * b);
@@ -168,19 +232,65 @@ struct XqView {
     }
 };
 
+// Rows of fp32 (written by other CTAs of this launch) into a q8_1 image in shared memory: one warp per 32-value block,
+// the reference's quantiser (the same bits as q8_1_lane / the standalone kernel).
+__device__ __forceinline__ void quantize_rows_to_smem(const float* src, int rows, int n, int8_t* codes, float* dsc,
+                                                      int warp, int lane, int nwarps) {
+    const int nb = n / 32;
+    for (int b = warp; b < rows * nb; b += nwarps) {
+        const int r = b / nb, k = b % nb;
+        const float v = __ldcg(src + (size_t) r * n + 32 * k + lane);
+        float d, sum;
+        const int8_t q = q8_1_warp(v, d, sum);
+        codes[(size_t) r * n + 32 * k + lane] = q;
+        if (lane == 0) dsc[b] = __half2float(__float2half(q8_finite(d)));
+    }
+}
+
+// IQ3_XXS row against nc <= 2 activations (dual-dp4a signs for one, materialised signs for two), calls lane + 32 j.
+template <int J>
+__device__ __forceinline__ void iq3_row(const uint8_t* row, int C, int lane, const Fmt<T_IQ3_XXS>::Act (&a)[2][J],
+                                        int nc, const AbsTab& t, float (&s)[2]) {
+    s[0] = s[1] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int k = lane + 32 * j;
+        if (k < C) {
+            const Iq3x x = iq3x_decode(row, k, t);
+            if (nc == 1) {
+                s[0] += iq3x_apply(x, a[0][j]);
+            } else {
+                const Fmt<T_IQ3_XXS>::W w = iq3x_signed(x);
+                s[0] += Fmt<T_IQ3_XXS>::apply(w, a[0][j]);
+                s[1] += Fmt<T_IQ3_XXS>::apply(w, a[1][j]);
+            }
+        }
+    }
+    s[0] = warp_sum(s[0]);
+    if (nc > 1) s[1] = warp_sum(s[1]);
+}
+
 // -------------------------------------------------------------------------------------------------- the kernel
 template <int V>   // V = E / 32 router values per lane
 __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* tab = smem;                                        // 64 KB lane-banked IQ3_XXS tables
-    uint8_t* ring = smem + kIqTabBytes;                         // kSlots x kSlotBytes
-    DecShared& S = *(DecShared*) (ring + (size_t) kSlots * kSlotBytes);
-    // [T][H] codes, read with 16-byte loads: 128-byte aligned past the shared state
-    int8_t* xq_codes = (int8_t*) (((uintptr_t) (&S + 1) + 127) & ~(uintptr_t) 127);
-    float* xq_d = (float*) (xq_codes + (size_t) p.T * p.H);     // [T][H / 32]
-    float* parts = xq_d + p.T * (p.H / 32);                     // [T * K][kDecMaxRows]
+    const DecSmem M = dec_smem(p.smem_base, p.T, p.H, p.F, p.FS, p.K);
+    uint8_t* ring = smem;
+    uint8_t* tab = smem + M.tab;
+    DecShared& S = *(DecShared*) (smem + M.shared);
+    float* parts = (float*) (smem + M.parts);
+    int8_t* xq_codes = (int8_t*) (smem + M.uni);
+    float* xq_d = (float*) (smem + M.xq_d);
+    int8_t* hs_codes = (int8_t*) (smem + M.hs);
+    float* hs_d = (float*) (smem + M.hs_d);
+    int8_t* hq_codes = (int8_t*) (smem + M.uni);   // P3 reuses the union
+    float* hq_d = (float*) (smem + M.hq_d);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (smem_u32(smem) != p.smem_base) {   // the layout assumes the base the host computed it for
+        if (threadIdx.x == 0) report_error(p.err, 0x300u);
+        return;
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(&S.full[s], 1);
@@ -189,6 +299,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         mbar_init(&S.route, 1);
         S.claim = 0;
         S.abort = 0;
+        S.prod_seq = 0;
+        S.prod_state = 0;
+        S.canary = 0xC0FFEE01u;
+        for (int q = 0; q < kSlots; ++q) S.slot_lap[q] = -1;
+        if (blockIdx.x == 0 && p.err) {   // the layout as the device sees it
+            p.err[110] = smem_u32(smem);
+            p.err[111] = smem_u32(tab);
+            p.err[112] = smem_u32(&S);
+            p.err[113] = smem_u32(parts);
+            p.err[114] = smem_u32(xq_codes);
+            p.err[115] = M.total;
+        }
         fence_mbar_init();
     }
     __syncthreads();
@@ -202,6 +324,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         pr.p = &p;
         for (int l = 0; l < p.n_layers && !S.abort; ++l) {
             const DecLayer L = p.layers[l];
+            S.prod_state = (l << 4) | 1;
             // P1
             const Range r1 = split(p1_units(p), gridDim.x, blockIdx.x);
             for (int u = r1.lo; u < r1.hi; ++u) {
@@ -211,19 +334,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 if (u < 2 * (p.E + 1)) {
                     const int o = u >> 1, half = u & 1;
                     const uint32_t nb = (uint32_t) (p.H / 2 * 4);
-                    mbar_expect_tx(&S.full[slot], nb);
+                    pr.start(slot); mbar_expect_tx(&S.full[slot], nb);
                     bulk_g2s(dst, L.router + (size_t) o * p.H + half * (p.H / 2), nb, &S.full[slot]);
                 } else {
                     const int r = u - 2 * (p.E + 1);
-                    mbar_expect_tx(&S.full[slot], 2 * p.sgu_row);
+                    pr.start(slot); mbar_expect_tx(&S.full[slot], 2 * p.sgu_row);
                     bulk_g2s(dst, L.sh_blob + (size_t) r * p.sgu_row, p.sgu_row, &S.full[slot]);
                     bulk_g2s(dst + p.sgu_row, L.sh_blob + p.s_up_off + (size_t) r * p.sgu_row, p.sgu_row, &S.full[slot]);
                 }
                 pr.finish(slot);
             }
             stamp(p, l, 9);
-            // wait for this layer's routing
-            {
+            S.prod_state = (l << 4) | 2;
+            {   // this layer's routing
                 const uint64_t t0 = globaltimer();
                 while (!mbar_try_wait(&S.route, (uint32_t) (l & 1))) {
                     if (globaltimer() - t0 > kWaitNs || S.abort) {
@@ -236,6 +359,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
             }
             const int ng = S.n_groups;
             stamp(p, l, 10);
+            S.prod_state = (l << 4) | 3 | (ng << 16);
             // P2
             const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
             const Range r2 = split(n2, gridDim.x, blockIdx.x);
@@ -245,7 +369,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 uint8_t* dst = pr.slot_ptr(slot);
                 if (u < nrt) {
                     const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * p.F);
-                    mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * 2 * p.gu_row);
+                    pr.start(slot); mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * 2 * p.gu_row);
                     for (int i = i0; i < i1; ++i) {
                         const int g = i / p.F, r = i % p.F;
                         const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + (size_t) r * p.gu_row;
@@ -256,12 +380,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 } else {
                     const int r0 = (u - nrt) * p.sd_per_unit;
                     const uint32_t nb = (uint32_t) p.sd_per_unit * p.sd_row;
-                    mbar_expect_tx(&S.full[slot], nb);
+                    pr.start(slot); mbar_expect_tx(&S.full[slot], nb);
                     bulk_g2s(dst, L.sh_blob + p.s_down_off + (size_t) r0 * p.sd_row, nb, &S.full[slot]);
                 }
                 pr.finish(slot);
             }
             stamp(p, l, 11);
+            S.prod_state = (l << 4) | 4 | (ng << 16);
             // P3
             const Range ch = my_chunks(p);
             const int ntask = (ch.hi - ch.lo) * ng;
@@ -272,7 +397,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 if (!pr.acquire(slot)) break;
                 uint8_t* dst = pr.slot_ptr(slot);
                 const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
-                mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * cb);
+                pr.start(slot); mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * cb);
                 for (int i = i0; i < i1; ++i) {
                     const int c = ch.lo + i / ng, g = i % ng;
                     const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + p.down_off + (size_t) c * cb;
@@ -295,12 +420,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     // ============================================================================================ consumers
     fill_tables<T_IQ3_XXS>(tab, kDecCThreads);   // consumers only, so a named barrier (not __syncthreads)
     named_sync(1, kDecCThreads);
+    if (threadIdx.x == 0 && S.canary != 0xC0FFEE01u) {
+        report_error(p.err, 0x3F0u);
+        if (p.err) p.err[116] = S.canary;
+    }
     const IqTab itab = make_tab(tab, lane);
+    const AbsTab atab = make_abs_tab(lane);
     uint32_t seq = 0;               // the ring sequence number of the next unit, identical in every consumer
     int claim_base = 0;
     unsigned target = 0;
     const int T = p.T, H = p.H, F = p.F, E = p.E, K = p.K;
     const XqView xv{xq_codes, xq_d, H};
+    const XqView hsv{hs_codes, hs_d, p.FS};
+    const XqView hqv{hq_codes, hq_d, F};
 
     auto claim = [&](int n, int& k) -> bool {   // this warp's next unit of the phase, or false
         int v = 0;
@@ -309,13 +441,54 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         k = v - claim_base;
         return k < n;
     };
+    int cur_layer = 0, cur_phase = 0;
     auto wait_full = [&](uint32_t s) -> bool {
         const uint32_t slot = s % kSlots, par = (s / kSlots) & 1u;
-        if (mbar_try_wait(&S.full[slot], par)) return true;
+        if (lane == 0) {
+            S.warp_unit[warp] = (int) s;
+            S.warp_state[warp] = 1;
+        }
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(&S.full[slot], par)) {
-            if (globaltimer() - t0 > kWaitNs || S.abort) {
-                report_error(p.err, 0x330u);
+        bool failed = false;
+        while (S.slot_lap[slot] < (int) (s / kSlots)) {   // the producer has not started this lap on the slot yet
+            if (globaltimer() - t0 > kWaitNs) {
+                failed = true;
+                break;
+            }
+        }
+        bool done = failed || mbar_try_wait(&S.full[slot], par);
+        while (!done) {   // every lane observes the phase itself (the bulk copy's bytes are then visible to it)
+            done = mbar_try_wait(&S.full[slot], par);
+            if (!done && globaltimer() - t0 > kWaitNs) {
+                failed = true;
+                break;
+            }
+        }
+        if (__all_sync(0xffffffffu, !failed)) {   // one verdict for the whole warp
+            if (lane == 0) S.warp_state[warp] = 2;
+            return true;
+        }
+        {
+            {
+                report_error(p.err, 0x330u | ((unsigned) cur_phase << 12));
+                if (p.err && atomicCAS(p.err + 61, 0u, 1u) == 0u) {
+                    p.err[1] = s | ((unsigned) cur_layer << 24);
+                    p.err[2] = (unsigned) S.prod_seq;
+                    p.err[3] = (unsigned) S.prod_state;
+                    p.err[4] = (unsigned) claim_base | (blockIdx.x << 20);
+                    p.err[5] = (unsigned) S.claim;
+                    for (int w = 0; w < kDecConsumers; ++w)
+                        p.err[6 + w] = (unsigned) S.warp_unit[w] | ((unsigned) S.warp_state[w] << 16);
+                    for (int q = 0; q < kSlots; ++q) {   // raw mbarrier words of every slot
+                        const unsigned long long f = *(volatile unsigned long long*) &S.full[q];
+                        const unsigned long long e = *(volatile unsigned long long*) &S.empty[q];
+                        p.err[24 + 4 * q] = (unsigned) f;
+                        p.err[25 + 4 * q] = (unsigned) (f >> 32);
+                        p.err[26 + 4 * q] = (unsigned) e;
+                        p.err[27 + 4 * q] = (unsigned) (e >> 32);
+                    }
+                    __threadfence();
+                }
                 S.abort = 1;
                 return false;
             }
@@ -324,7 +497,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     };
     auto release = [&](uint32_t s) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[s % kSlots]);
+        if (lane == 0) {
+            mbar_arrive(&S.empty[s % kSlots]);
+            S.warp_state[warp] = 3;
+        }
     };
     auto end_phase = [&](int n) {   // every consumer warp overshoots its claims once
         claim_base += n + kDecConsumers;
@@ -339,22 +515,32 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     for (int l = 0; l < p.n_layers; ++l) {
         if (threadIdx.x == 0) stamp(p, l, 0);
         // ---------------------------------------------------------------- P0: rms and q8_1 of every token
+        // The reference's order (k_moe_out_small): 256 slots s = sum over i = s mod 256 of x_i^2 in order, then the
+        // halving tree; thread i < 32 forms the tree's 32-slot level from 8 slots, shuffles finish it.
         for (int t = 0; t < T; ++t) {
             const float* xr = p.x + (size_t) t * H;
             if (threadIdx.x < 256) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = threadIdx.x + 256 * k < H ? __ldcg(xr + threadIdx.x + 256 * k) : 0.0f;
                 float s = 0.0f;
-                for (int i = threadIdx.x; i < H; i += 256) {
-                    const float v = __ldcg(xr + i);
-                    s += v * v;
+                for (int k = 0; k < 8 && threadIdx.x + 256 * k < H; ++k) s += v[k] * v[k];
+                for (int i = threadIdx.x + 2048; i < H; i += 256) {
+                    const float x = __ldcg(xr + i);
+                    s += x * x;
                 }
                 S.red[threadIdx.x] = s;
             }
             named_sync(1, kDecCThreads);
-            for (int o = 128; o > 0; o >>= 1) {
-                if ((int) threadIdx.x < o) S.red[threadIdx.x] += S.red[threadIdx.x + o];
-                named_sync(1, kDecCThreads);
+            if (warp == 0) {
+                const float* r = S.red;
+                const int i = lane;
+                float a = ((r[i] + r[i + 128]) + (r[i + 64] + r[i + 192])) +
+                          ((r[i + 32] + r[i + 160]) + (r[i + 96] + r[i + 224]));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a += __shfl_down_sync(0xffffffffu, a, o);
+                if (lane == 0) S.rms[t] = rsqrtf(fdiv_fm(a, (float) H) + p.eps);
             }
-            if (threadIdx.x == 0) S.rms[t] = rsqrtf(fdiv_fm(S.red[0], (float) H) + p.eps);
             named_sync(1, kDecCThreads);
             const float r = S.rms[t];
             for (int b = warp; b < H / 32; b += kDecConsumers) {
@@ -364,10 +550,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 xq_codes[(size_t) t * H + 32 * b + lane] = q;
                 if (lane == 0) xq_d[t * (H / 32) + b] = __half2float(__float2half(q8_finite(d)));
             }
-            named_sync(1, kDecCThreads);
         }
-
+        named_sync(1, kDecCThreads);
         if (threadIdx.x == 0) stamp(p, l, 1);
+        cur_layer = l;
+        cur_phase = 1;
+
         // ---------------------------------------------------------------- P1: router rows, shared gate/up
         {
             const int n1 = p1_units(p);
@@ -386,6 +574,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         const float* xr = p.x + (size_t) t * H + half * (H / 2);
                         const float r = S.rms[t];
                         float acc = 0.0f;
+#pragma unroll 4
                         for (int i = lane; i < H / 8; i += 32) {
                             const float4 w = wr[i];
                             const float4 xv4 = __ldcg((const float4*) xr + i);
@@ -419,8 +608,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         if (!grid_barrier(p, S, target, 0x340u)) break;
         if (threadIdx.x == 0) stamp(p, l, 3);
 
-        // ---------------------------------------------------------------- R: routing and grouping
-        for (int t = warp; t < T; t += kDecConsumers) {   // 15 consumer warps: token 15 goes round again
+        // ---------------------------------------------------------------- R: routing, grouping; shared hidden -> q8_1
+        for (int t = warp; t < T; t += kDecConsumers) {
             const float* lg = p.logits + (size_t) t * (E + 1) * 2;
             float values[V];
 #pragma unroll
@@ -480,6 +669,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 S.gs[t] = frcp_fm(1.0f + fexp_fm(-(pg.x + pg.y)));
             }
         }
+        // the shared expert's hidden vectors into q8_1 (warps after the routing ones)
+        quantize_rows_to_smem(p.hsh, T, p.FS, hs_codes, hs_d, (warp + kDecConsumers - T % kDecConsumers) % kDecConsumers,
+                              lane, kDecConsumers);
         named_sync(1, kDecCThreads);
         {
             const int n_ent = T * K;
@@ -499,8 +691,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 }
             }
             named_sync(1, kDecCThreads);
-            // group g starts at the sorted position of the first entry of its expert
-            if (e < n_ent) {
+            if (e < n_ent) {   // group g starts at the sorted position of the first entry of its expert
                 const int pos = rank;
                 const int prev_id = pos > 0 ? S.ids[S.ent_dst[pos - 1]] : -1;
                 if (prev_id != id) {
@@ -523,6 +714,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         if (threadIdx.x == 0) stamp(p, l, 4);
 
         // ---------------------------------------------------------------- P2: routed gate/up, shared down
+        cur_phase = 2;
         {
             const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
             const Range r2 = split(n2, gridDim.x, blockIdx.x);
@@ -542,7 +734,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
                         for (int eb = e0; eb < e1; eb += 2) {
                             const int nc = min(2, e1 - eb);
-                            typename Fmt<T_IQ3_XXS>::Act a[2][2];
+                            Fmt<T_IQ3_XXS>::Act a[2][2];
 #pragma unroll
                             for (int c = 0; c < 2; ++c) {
                                 if (c >= nc) break;
@@ -553,12 +745,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                                     if (lane + 32 * j < Cg) a[c][j] = Fmt<T_IQ3_XXS>::act(src, lane + 32 * j);
                             }
                             float sg[2], su[2];
-                            row_dot<T_IQ3_XXS, 2, 2>(gate, Cg, lane, a, nc, itab, sg);
-                            row_dot<T_IQ3_XXS, 2, 2>(up, Cg, lane, a, nc, itab, su);
-#pragma unroll
-                            for (int c = 0; c < 2; ++c)
-                                if (c < nc && lane == c)
-                                    p.hbuf[(size_t) S.ent_dst[eb + c] * F + r] = act_value(ACT_SWIGLU, sg[c], su[c], INFINITY);
+                            iq3_row<2>(gate, Cg, lane, a, nc, atab, sg);
+                            iq3_row<2>(up, Cg, lane, a, nc, atab, su);
+                            if (lane < nc)
+                                p.hbuf[(size_t) S.ent_dst[eb + lane] * F + r] =
+                                    act_value(ACT_SWIGLU, lane == 0 ? sg[0] : sg[1], lane == 0 ? su[0] : su[1], INFINITY);
                         }
                     }
                 } else {
@@ -569,8 +760,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
 #pragma unroll
                         for (int c = 0; c < 2; ++c) {
                             if (c >= nc) break;
-                            const float* hx = p.hsh + (size_t) (t0 + c) * p.FS;
-                            auto src = [&](int blk) { return qb_from_f32_cg(hx + 32 * blk); };
+                            auto src = [&](int blk) { return hsv.block(t0 + c, blk); };
 #pragma unroll
                             for (int j = 0; j < 2; ++j)
                                 if (lane + 32 * j < Csd) a[c][j] = Fmt<T_Q8_0>::act(src, lane + 32 * j);
@@ -591,11 +781,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         if (threadIdx.x == 0) stamp(p, l, 6);
 
         // ---------------------------------------------------------------- P3: routed down rows, combine
+        cur_phase = 3;
         {
+            quantize_rows_to_smem(p.hbuf, T * K, F, hq_codes, hq_d, warp, lane, kDecConsumers);
+            named_sync(1, kDecCThreads);
             const Range ch = my_chunks(p);
             const int ntask = (ch.hi - ch.lo) * ng;
             const int mine = p3_units(p, ng);
             const int P = 32 / Cd;   // rows per pass (Cd = 16 -> 2)
+            const int rl = lane / Cd, kc = lane % Cd;
             int k;
             while (claim(mine, k)) {
                 const uint32_t s = seq + (uint32_t) k;
@@ -606,24 +800,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     const int cl = i / ng, g = i % ng;   // chunk index within this CTA, group
                     const uint8_t* rows = buf + (size_t) (i - i0) * p.R * p.d_row;
                     const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
-                    for (int eb = e0; eb < e1; eb += 4) {
-                        const int nc = min(4, e1 - eb);
-                        typename Fmt<T_IQ3_XXS>::Act a[4][1];
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            if (c >= nc) break;
-                            const float* hx = p.hbuf + (size_t) S.ent_dst[eb + c] * F;
-                            auto src = [&](int blk) { return qb_from_f32_cg(hx + 32 * blk); };
-                            a[c][0] = Fmt<T_IQ3_XXS>::act(src, lane % Cd);
-                        }
+                    for (int eb = e0; eb < e1; ++eb) {
+                        const int ent = S.ent_dst[eb];
+                        auto src = [&](int blk) { return hqv.block(ent, blk); };
+                        const Fmt<T_IQ3_XXS>::Act a = Fmt<T_IQ3_XXS>::act(src, kc);
                         for (int rr = 0; rr < p.R; rr += P) {
-                            float sv[4];
-                            row_dot_packed<T_IQ3_XXS, 4>(rows + (size_t) rr * p.d_row, p.d_row, Cd, lane, a, nc, itab, sv);
-                            const int rl = lane / Cd, cl2 = lane % Cd;
-#pragma unroll
-                            for (int c = 0; c < 4; ++c)
-                                if (c < nc && cl2 == c)
-                                    parts[S.ent_dst[eb + c] * kDecMaxRows + cl * p.R + rr + rl] = sv[c];
+                            const Iq3x x = iq3x_decode(rows + (size_t) (rr + rl) * p.d_row, kc, atab);
+                            float v = iq3x_apply(x, a);
+                            for (int o = Cd >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                            if (kc == 0) parts[ent * kDecMaxRows + cl * p.R + rr + rl] = v;
                         }
                     }
                 }

@@ -349,6 +349,87 @@ template <> struct Fmt<T_Q6_K> {
     }
 };
 
+
+// ------------------------------------------------------------------------------------------------ IQ3_XXS, absolute
+// The fused decode kernel keeps the lane-banked tables at shared-window address 0x10000, so one byte_perm of a code
+// word with (0x10000 | 4 lane) is the full address of a grid entry and the sign-mask address is a shift and a
+// three-input op; `ld.shared` takes them as they are.
+constexpr uint32_t kAbsTab = 0x10000u;
+struct AbsTab {
+    uint32_t lane_g;   // kAbsTab | 4 lane
+    uint32_t lane_s;   // kAbsTab | 128 | 8 (lane & 15)
+};
+__device__ __forceinline__ AbsTab make_abs_tab(int lane) {
+    return {kAbsTab | (4u * (uint32_t) lane), kAbsTab | 128u | (8u * (uint32_t) (lane & 15))};
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds_u64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+// the sign-mask address of 7-bit field l of aux: ((aux >> 7 l) & 127) << 8 | lane_s
+template <int L> __device__ __forceinline__ uint32_t sign_addr(uint32_t aux, uint32_t lane_s) {
+    constexpr int sh = 7 * L - 8;
+    const uint32_t t = sh >= 0 ? (aux >> sh) : (aux << -sh);
+    return (t & 0x7F00u) | lane_s;
+}
+// One IQ3_XXS call, decoded with the signs still separate: gx = grid ^ mask, m = mask (0xFF bytes where negative).
+// sum(sign * grid * u) = dp4a(gx, u) - dp4a(m, u): (g ^ 0xFF) is -g - 1 as a signed byte and m is -1.
+struct Iq3x {
+    uint32_t gx[8], m[8];
+    int ls;
+    float dw;
+};
+__device__ __forceinline__ Iq3x iq3x_decode(const uint8_t* row, int call, const AbsTab& t) {
+    const uint8_t* wb = row + (call >> 3) * 98;
+    const int c = call & 7;
+    const uint32_t q0 = lw2(wb + 2 + 8 * c), q1 = lw2(wb + 6 + 8 * c), aux = lw2(wb + 66 + 4 * c);
+    Iq3x w;
+    const uint2 m0 = lds_u64(sign_addr<0>(aux, t.lane_s)), m1 = lds_u64(sign_addr<1>(aux, t.lane_s));
+    const uint2 m2 = lds_u64(sign_addr<2>(aux, t.lane_s)), m3 = lds_u64(sign_addr<3>(aux, t.lane_s));
+    w.m[0] = m0.x; w.m[1] = m0.y; w.m[2] = m1.x; w.m[3] = m1.y;
+    w.m[4] = m2.x; w.m[5] = m2.y; w.m[6] = m3.x; w.m[7] = m3.y;
+    w.gx[0] = lds_u32(prmt(q0, t.lane_g, 0x7604u)) ^ w.m[0];
+    w.gx[1] = lds_u32(prmt(q0, t.lane_g, 0x7614u)) ^ w.m[1];
+    w.gx[2] = lds_u32(prmt(q0, t.lane_g, 0x7624u)) ^ w.m[2];
+    w.gx[3] = lds_u32(prmt(q0, t.lane_g, 0x7634u)) ^ w.m[3];
+    w.gx[4] = lds_u32(prmt(q1, t.lane_g, 0x7604u)) ^ w.m[4];
+    w.gx[5] = lds_u32(prmt(q1, t.lane_g, 0x7614u)) ^ w.m[5];
+    w.gx[6] = lds_u32(prmt(q1, t.lane_g, 0x7624u)) ^ w.m[6];
+    w.gx[7] = lds_u32(prmt(q1, t.lane_g, 0x7634u)) ^ w.m[7];
+    w.ls = (int) (aux >> 28);
+    w.dw = lh(wb);
+    return w;
+}
+__device__ __forceinline__ int iq3x_sumi(const Iq3x& w, const int (&u)[8]) {
+    int a = 0, b = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        a = dp4a((int) w.gx[j], u[j], a);
+        b = dp4a((int) w.m[j], u[j], b);
+    }
+    const int s = a - b;
+    return (w.ls * s + s / 2) / 2;
+}
+__device__ __forceinline__ float iq3x_apply(const Iq3x& w, const Fmt<T_IQ3_XXS>::Act& a) {
+    const float d = w.dw * a.d;
+    return d * (float) iq3x_sumi(w, a.u);
+}
+// materialised signed codes (several tokens per decoded call)
+__device__ __forceinline__ Fmt<T_IQ3_XXS>::W iq3x_signed(const Iq3x& x) {
+    Fmt<T_IQ3_XXS>::W w;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w.v[j] = (int) (x.gx[j] + (x.m[j] & 0x01010101u));
+    w.ls = x.ls;
+    w.dw = x.dw;
+    return w;
+}
+
 // Dispatch helper so every decode has one signature: IQ3_S reads its plain 512-word grid at t.base + kIqTabBytes.
 template <int TY> __device__ __forceinline__ typename Fmt<TY>::W decode_call(const uint8_t* row, int call, const IqTab& t) {
     if constexpr (TY == T_IQ3_S) return Fmt<TY>::decode(row, call, (const uint32_t*) (t.base + kIqTabBytes));
