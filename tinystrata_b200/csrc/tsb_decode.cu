@@ -45,8 +45,8 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     const int T = d->n_tok, H = d->n_embd, F = d->n_ff, E = d->n_expert, K = d->n_used, FS = d->sh_n_ff;
     if (T < 1 || T > kDecMaxT || K < 1 || T * K > kDecMaxEnt || E < 32 || E % 32 || E / 32 != 8 || K > E)
         return dfail(TSB_ERR_UNSUPPORTED, "decode: 1..16 tokens, 256 experts, T*K <= 128");
-    if (H % 256 || F % 256 || FS % 32 || H / 2 * 4 > (int) kSlotBytes || F != 512)
-        return dfail(TSB_ERR_UNSUPPORTED, "decode: hidden a multiple of 256 up to 2176, expert FF 512");
+    if (H % 2048 || H > 2048 || F != 512 || FS % 128)
+        return dfail(TSB_ERR_UNSUPPORTED, "decode: hidden 2048, expert FF 512, shared FF a multiple of 128");
     p.n_layers = d->n_layers;
     p.T = T; p.H = H; p.F = F; p.E = E; p.K = K; p.FS = FS;
     p.gu_row = (uint32_t) (H / 256 * 98);
@@ -58,9 +58,7 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     p.sd_row = (uint32_t) (FS / 32 * 34);
     p.s_up_off = (uint64_t) FS * p.sgu_row;
     p.s_down_off = 2 * p.s_up_off;
-    p.R = 1;
-    while ((p.R * p.d_row) % 16) p.R *= 2;
-    if (p.R < 2) p.R = 2;   // two rows per pass of 16 calls
+    p.R = 4;   // four rows per routed down task: one pass of 32 lanes over their two blocks each (F = 512)
     p.rt_per_unit = (int) (kSlotBytes / (2 * p.gu_row));
     p.sd_per_unit = (int) (kSlotBytes / p.sd_row);
     while (p.sd_per_unit > 1 && H % p.sd_per_unit) --p.sd_per_unit;

@@ -247,6 +247,75 @@ __device__ __forceinline__ void quantize_rows_to_smem(const float* src, int rows
     }
 }
 
+// A contiguous fp32 array (rows of 32-value blocks; written by other CTAs of this launch, or in shared memory) into
+// q8_1 codes and fp16-rounded scales in shared memory: 8 lanes per block, 4 values each (float4), up to 4 loads in
+// flight per lane before any arithmetic.  The block scale is amax / 127 with the reference's division and the codes
+// round(x / d): the same codes and scale as the reference's quantiser, whatever the lane layout (the fp16 sum it also
+// stores is not formed: no format here reads it).
+template <bool FROM_SMEM>
+__device__ __forceinline__ void quantize_blocks(const float* src, int n, int8_t* codes, float* dsc, int warp, int lane,
+                                                int nwarps) {
+    const int n4 = n / 4;
+    const int stride = nwarps * 32;
+    constexpr int B = 4;
+    for (int base = warp * 32 + lane; base - lane < n4; base += B * stride) {
+        float4 v[B];
+#pragma unroll
+        for (int it = 0; it < B; ++it) {
+            const int i = base + it * stride;
+            if (i < n4) v[it] = FROM_SMEM ? ((const float4*) src)[i] : __ldcg((const float4*) src + i);
+        }
+#pragma unroll
+        for (int it = 0; it < B; ++it) {
+            const int i = base + it * stride;
+            if (i - lane >= n4) break;   // warp-uniform: whole warps of float4s
+            float amax = fmaxf(fmaxf(fabsf(v[it].x), fabsf(v[it].y)), fmaxf(fabsf(v[it].z), fabsf(v[it].w)));
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float d = q8_finite(fdiv_fm(amax, 127.0f));
+            uint32_t word = 0;
+            const float xs[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int8_t c = 0;
+                if (amax != 0.0f) {
+                    const float r = roundf(fdiv_fm(xs[j], d));
+                    c = (int8_t) (r > 127.0f ? 127.0f : r < -127.0f ? -127.0f : r);
+                }
+                word |= (uint32_t) (uint8_t) c << (8 * j);
+            }
+            ((uint32_t*) codes)[i] = word;
+            if ((lane & 7) == 0) dsc[i >> 3] = __half2float(__float2half(d));
+        }
+    }
+}
+
+// IQ3_XXS gate/up row of 8 blocks (H = 2048) against one activation, with the block parity uniform per step: lane
+// l = 8 q + c decodes call c of block 2 q (step 0, 4-byte aligned) and of block 2 q + 1 (step 1, 2 mod 4); a[j] is the
+// q8_1 block of that call (iq3_par_call).  The sum has the bits of the reference's row order -- lane L adds call L's
+// product and then call L + 32's (multiply-add), an xor tree over 32 lanes -- rebuilt by exchanges: lanes 16..31 hold
+// the calls 32..63, take the products of calls 0..31 from lane l ^ 16 and form the 32 lane sums two per lane (blocks
+// even / odd), whose xor-16 level is a xor-8 exchange here and whose xor-8 level an add in the lane.  Every lane
+// returns the sum (lanes 0..15 a value of no use).
+__device__ __forceinline__ float iq3_row_par(const uint8_t* row, int lane, const Fmt<T_IQ3_XXS>::Act (&a)[2],
+                                             const AbsTab& t) {
+    const int c = lane & 7, q = lane >> 3;
+    const Iq3x xe = iq3x_decode_blk<false>(row + 196 * q, c, t);
+    const float de = __fmul_rn(xe.dw, a[0].d), fe = (float) iq3x_sumi(xe, a[0].u);
+    const Iq3x xo = iq3x_decode_blk<true>(row + 196 * q + 98, c, t);
+    const float dd = __fmul_rn(xo.dw, a[1].d), fo = (float) iq3x_sumi(xo, a[1].u);
+    const float pe = __shfl_xor_sync(0xffffffffu, __fmul_rn(de, fe), 16);
+    const float po = __shfl_xor_sync(0xffffffffu, __fmul_rn(dd, fo), 16);
+    float se = __fmaf_rn(de, fe, pe), so = __fmaf_rn(dd, fo, po);
+    se = __fadd_rn(se, __shfl_xor_sync(0xffffffffu, se, 8));
+    so = __fadd_rn(so, __shfl_xor_sync(0xffffffffu, so, 8));
+    float s = __fadd_rn(se, so);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    return s;
+}
+__device__ __forceinline__ int iq3_par_call(int lane, int j) { return 16 * (lane >> 3) + 8 * j + (lane & 7); }
+
 // IQ3_XXS row against nc <= 2 activations (dual-dp4a signs for one, materialised signs for two), calls lane + 32 j.
 template <int J>
 __device__ __forceinline__ void iq3_row(const uint8_t* row, int C, int lane, const Fmt<T_IQ3_XXS>::Act (&a)[2][J],
@@ -507,28 +576,22 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         seq += (uint32_t) n;
     };
 
-    const int Cg = H / 256 * 8;          // IQ3_XXS calls per gate/up row (64 at H = 2048)
     const int Cs = H / 32 * 4;           // Q8_0 calls per shared gate/up row
     const int Csd = p.FS / 32 * 4;       // Q8_0 calls per shared down row
-    const int Cd = F / 256 * 8;          // IQ3_XXS calls per routed down row (16 at F = 512)
 
     for (int l = 0; l < p.n_layers; ++l) {
         if (threadIdx.x == 0) stamp(p, l, 0);
         // ---------------------------------------------------------------- P0: rms and q8_1 of every token
         // The reference's order (k_moe_out_small): 256 slots s = sum over i = s mod 256 of x_i^2 in order, then the
         // halving tree; thread i < 32 forms the tree's 32-slot level from 8 slots, shuffles finish it.
+        float* xs = parts;   // the token's row in shared memory (the parts buffer is free until P3)
         for (int t = 0; t < T; ++t) {
             const float* xr = p.x + (size_t) t * H;
+            for (int i = threadIdx.x; i < H / 4; i += kDecCThreads) ((float4*) xs)[i] = __ldcg((const float4*) xr + i);
+            named_sync(1, kDecCThreads);
             if (threadIdx.x < 256) {
-                float v[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = threadIdx.x + 256 * k < H ? __ldcg(xr + threadIdx.x + 256 * k) : 0.0f;
                 float s = 0.0f;
-                for (int k = 0; k < 8 && threadIdx.x + 256 * k < H; ++k) s += v[k] * v[k];
-                for (int i = threadIdx.x + 2048; i < H; i += 256) {
-                    const float x = __ldcg(xr + i);
-                    s += x * x;
-                }
+                for (int i = threadIdx.x; i < H; i += 256) s += xs[i] * xs[i];
                 S.red[threadIdx.x] = s;
             }
             named_sync(1, kDecCThreads);
@@ -543,13 +606,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
             }
             named_sync(1, kDecCThreads);
             const float r = S.rms[t];
-            for (int b = warp; b < H / 32; b += kDecConsumers) {
-                const float hv = __fmul_rn(__ldcg(xr + 32 * b + lane), r);
-                float d, sum;
-                const int8_t q = q8_1_warp(hv, d, sum);
-                xq_codes[(size_t) t * H + 32 * b + lane] = q;
-                if (lane == 0) xq_d[t * (H / 32) + b] = __half2float(__float2half(q8_finite(d)));
-            }
+            for (int i = threadIdx.x; i < H; i += kDecCThreads) xs[i] = __fmul_rn(xs[i], r);   // h = x r (wn = 1)
+            named_sync(1, kDecCThreads);
+            quantize_blocks<true>(xs, H, xq_codes + (size_t) t * H, xq_d + t * (H / 32), warp, lane, kDecConsumers);
+            if (t + 1 < T) named_sync(1, kDecCThreads);
         }
         named_sync(1, kDecCThreads);
         if (threadIdx.x == 0) stamp(p, l, 1);
@@ -574,12 +634,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         const float* xr = p.x + (size_t) t * H + half * (H / 2);
                         const float r = S.rms[t];
                         float acc = 0.0f;
+                        if (T == 1) {   // h of the only token is in shared memory
+                            const float4* hs4 = (const float4*) (xs + half * (H / 2));
 #pragma unroll 4
-                        for (int i = lane; i < H / 8; i += 32) {
-                            const float4 w = wr[i];
-                            const float4 xv4 = __ldcg((const float4*) xr + i);
-                            acc += w.x * __fmul_rn(xv4.x, r) + w.y * __fmul_rn(xv4.y, r) + w.z * __fmul_rn(xv4.z, r) +
-                                   w.w * __fmul_rn(xv4.w, r);
+                            for (int i = lane; i < H / 8; i += 32) {
+                                const float4 w = wr[i], hv = hs4[i];
+                                acc += w.x * hv.x + w.y * hv.y + w.z * hv.z + w.w * hv.w;
+                            }
+                        } else {
+#pragma unroll 4
+                            for (int i = lane; i < H / 8; i += 32) {
+                                const float4 w = wr[i];
+                                const float4 xv4 = __ldcg((const float4*) xr + i);
+                                acc += w.x * __fmul_rn(xv4.x, r) + w.y * __fmul_rn(xv4.y, r) + w.z * __fmul_rn(xv4.z, r) +
+                                       w.w * __fmul_rn(xv4.w, r);
+                            }
                         }
                         acc = warp_sum(acc);
                         if (lane == 0) p.logits[((size_t) t * (E + 1) + o) * 2 + half] = acc;
@@ -669,9 +738,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 S.gs[t] = frcp_fm(1.0f + fexp_fm(-(pg.x + pg.y)));
             }
         }
-        // the shared expert's hidden vectors into q8_1 (warps after the routing ones)
-        quantize_rows_to_smem(p.hsh, T, p.FS, hs_codes, hs_d, (warp + kDecConsumers - T % kDecConsumers) % kDecConsumers,
-                              lane, kDecConsumers);
+        // the shared expert's hidden vectors into q8_1, by the warps that route no token
+        if (T < kDecConsumers && warp >= T)
+            quantize_blocks<false>(p.hsh, T * p.FS, hs_codes, hs_d, warp - T, lane, kDecConsumers - T);
+        else if (T >= kDecConsumers)
+            quantize_blocks<false>(p.hsh, T * p.FS, hs_codes, hs_d, warp, lane, kDecConsumers);
         named_sync(1, kDecCThreads);
         {
             const int n_ent = T * K;
@@ -732,24 +803,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         const uint8_t* gate = buf + (size_t) (i - i0) * 2 * p.gu_row;
                         const uint8_t* up = gate + p.gu_row;
                         const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
-                        for (int eb = e0; eb < e1; eb += 2) {
-                            const int nc = min(2, e1 - eb);
-                            Fmt<T_IQ3_XXS>::Act a[2][2];
+                        for (int eb = e0; eb < e1; ++eb) {   // decode groups rarely hold more than one entry
+                            const int tok = S.ent_tok[eb];
+                            auto src = [&](int blk) { return xv.block(tok, blk); };
+                            Fmt<T_IQ3_XXS>::Act a[2];
 #pragma unroll
-                            for (int c = 0; c < 2; ++c) {
-                                if (c >= nc) break;
-                                const int tok = S.ent_tok[eb + c];
-                                auto src = [&](int blk) { return xv.block(tok, blk); };
-#pragma unroll
-                                for (int j = 0; j < 2; ++j)
-                                    if (lane + 32 * j < Cg) a[c][j] = Fmt<T_IQ3_XXS>::act(src, lane + 32 * j);
-                            }
-                            float sg[2], su[2];
-                            iq3_row<2>(gate, Cg, lane, a, nc, atab, sg);
-                            iq3_row<2>(up, Cg, lane, a, nc, atab, su);
-                            if (lane < nc)
-                                p.hbuf[(size_t) S.ent_dst[eb + lane] * F + r] =
-                                    act_value(ACT_SWIGLU, lane == 0 ? sg[0] : sg[1], lane == 0 ? su[0] : su[1], INFINITY);
+                            for (int j = 0; j < 2; ++j) a[j] = Fmt<T_IQ3_XXS>::act(src, iq3_par_call(lane, j));
+                            const float sg = iq3_row_par(gate, lane, a, atab);
+                            const float su = iq3_row_par(up, lane, a, atab);
+                            if (lane == 16) p.hbuf[(size_t) S.ent_dst[eb] * F + r] = act_value(ACT_SWIGLU, sg, su, INFINITY);
                         }
                     }
                 } else {
@@ -783,13 +845,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         // ---------------------------------------------------------------- P3: routed down rows, combine
         cur_phase = 3;
         {
-            quantize_rows_to_smem(p.hbuf, T * K, F, hq_codes, hq_d, warp, lane, kDecConsumers);
+            quantize_blocks<false>(p.hbuf, T * K * F, hq_codes, hq_d, warp, lane, kDecConsumers);
             named_sync(1, kDecCThreads);
             const Range ch = my_chunks(p);
             const int ntask = (ch.hi - ch.lo) * ng;
             const int mine = p3_units(p, ng);
-            const int P = 32 / Cd;   // rows per pass (Cd = 16 -> 2)
-            const int rl = lane / Cd, kc = lane % Cd;
             int k;
             while (claim(mine, k)) {
                 const uint32_t s = seq + (uint32_t) k;
@@ -803,13 +863,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     for (int eb = e0; eb < e1; ++eb) {
                         const int ent = S.ent_dst[eb];
                         auto src = [&](int blk) { return hqv.block(ent, blk); };
-                        const Fmt<T_IQ3_XXS>::Act a = Fmt<T_IQ3_XXS>::act(src, kc);
-                        for (int rr = 0; rr < p.R; rr += P) {
-                            const Iq3x x = iq3x_decode(rows + (size_t) (rr + rl) * p.d_row, kc, atab);
-                            float v = iq3x_apply(x, a);
-                            for (int o = Cd >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                            if (kc == 0) parts[ent * kDecMaxRows + cl * p.R + rr + rl] = v;
-                        }
+                        const Fmt<T_IQ3_XXS>::Act a0 = Fmt<T_IQ3_XXS>::act(src, lane & 7);
+                        const Fmt<T_IQ3_XXS>::Act a1 = Fmt<T_IQ3_XXS>::act(src, 8 + (lane & 7));
+                        // 4 rows of 2 blocks (F = 512): block 0 of row r at 196 r (0 mod 4), block 1 at 196 r + 98.  The
+                        // reference's row sum is an xor tree over 16 lanes of one call each: its first level (calls c and
+                        // c + 8) is the add in the lane here, the rest the same exchanges.
+                        const uint8_t* rw = rows + (size_t) (lane >> 3) * p.d_row;
+                        const Iq3x x0 = iq3x_decode_blk<false>(rw, lane & 7, atab);
+                        const float v0 = __fmul_rn(__fmul_rn(x0.dw, a0.d), (float) iq3x_sumi(x0, a0.u));
+                        const Iq3x x1 = iq3x_decode_blk<true>(rw + 98, lane & 7, atab);
+                        float v = __fadd_rn(v0, __fmul_rn(__fmul_rn(x1.dw, a1.d), (float) iq3x_sumi(x1, a1.u)));
+#pragma unroll
+                        for (int o = 4; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                        if ((lane & 7) == 0) parts[ent * kDecMaxRows + cl * p.R + (lane >> 3)] = v;
                     }
                 }
                 release(s);

@@ -430,6 +430,43 @@ __device__ __forceinline__ Fmt<T_IQ3_XXS>::W iq3x_signed(const Iq3x& x) {
     return w;
 }
 
+
+// The same decode with the block's alignment known at compile time (rows staged 4-byte aligned): a block at an even
+// position of its row starts at 0 mod 4, an odd one at 2 mod 4 (98-byte blocks).  Aligned 32-bit loads and byte_perm
+// replace the 16-bit loads.
+template <bool ODD>
+__device__ __forceinline__ Iq3x iq3x_decode_blk(const uint8_t* wb, int c, const AbsTab& t) {
+    uint32_t q0, q1, aux;
+    if constexpr (ODD) {
+        q0 = *(const uint32_t*) (wb + 2 + 8 * c);
+        q1 = *(const uint32_t*) (wb + 6 + 8 * c);
+        aux = *(const uint32_t*) (wb + 66 + 4 * c);
+    } else {
+        const uint32_t* w = (const uint32_t*) (wb + 8 * c);
+        const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+        q0 = prmt(w0, w1, 0x5432u);
+        q1 = prmt(w1, w2, 0x5432u);
+        const uint32_t* a = (const uint32_t*) (wb + 64 + 4 * c);
+        aux = prmt(a[0], a[1], 0x5432u);
+    }
+    Iq3x w;
+    const uint2 m0 = lds_u64(sign_addr<0>(aux, t.lane_s)), m1 = lds_u64(sign_addr<1>(aux, t.lane_s));
+    const uint2 m2 = lds_u64(sign_addr<2>(aux, t.lane_s)), m3 = lds_u64(sign_addr<3>(aux, t.lane_s));
+    w.m[0] = m0.x; w.m[1] = m0.y; w.m[2] = m1.x; w.m[3] = m1.y;
+    w.m[4] = m2.x; w.m[5] = m2.y; w.m[6] = m3.x; w.m[7] = m3.y;
+    w.gx[0] = lds_u32(prmt(q0, t.lane_g, 0x7604u)) ^ w.m[0];
+    w.gx[1] = lds_u32(prmt(q0, t.lane_g, 0x7614u)) ^ w.m[1];
+    w.gx[2] = lds_u32(prmt(q0, t.lane_g, 0x7624u)) ^ w.m[2];
+    w.gx[3] = lds_u32(prmt(q0, t.lane_g, 0x7634u)) ^ w.m[3];
+    w.gx[4] = lds_u32(prmt(q1, t.lane_g, 0x7604u)) ^ w.m[4];
+    w.gx[5] = lds_u32(prmt(q1, t.lane_g, 0x7614u)) ^ w.m[5];
+    w.gx[6] = lds_u32(prmt(q1, t.lane_g, 0x7624u)) ^ w.m[6];
+    w.gx[7] = lds_u32(prmt(q1, t.lane_g, 0x7634u)) ^ w.m[7];
+    w.ls = (int) (aux >> 28);
+    w.dw = lh(wb);
+    return w;
+}
+
 // Dispatch helper so every decode has one signature: IQ3_S reads its plain 512-word grid at t.base + kIqTabBytes.
 template <int TY> __device__ __forceinline__ typename Fmt<TY>::W decode_call(const uint8_t* row, int call, const IqTab& t) {
     if constexpr (TY == T_IQ3_S) return Fmt<TY>::decode(row, call, (const uint32_t*) (t.base + kIqTabBytes));
