@@ -1,4 +1,5 @@
 // tsb_decode.cu - host side of the fused decode kernel (tsb_decode.cuh): validation, workspace, cooperative launch.
+#include <algorithm>
 #include "tsb_decode.cuh"
 #include "../../include/tsb_moe.h"
 
@@ -62,8 +63,9 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     p.rt_per_unit = (int) (kSlotBytes / (2 * p.gu_row));
     p.sd_per_unit = (int) (kSlotBytes / p.sd_row);
     while (p.sd_per_unit > 1 && H % p.sd_per_unit) --p.sd_per_unit;
-    p.dn_per_unit = (int) (kSlotBytes / (p.R * p.d_row));
-    if (p.gu_row % 16 || p.sgu_row % 16 || p.sd_row % 16 || p.blob_bytes % 16 || p.rt_per_unit < 1 ||
+    // Two routed down tasks (4 rows of one expert each) per slot: about one unit per consumer warp at T = 1.
+    p.dn_per_unit = std::min(2, (int) (kSlotBytes / (p.R * p.d_row)));
+    if (p.gu_row % 16 || p.sgu_row % 16 || p.sd_row % 16 || p.blob_bytes % 16 || p.rt_per_unit < 1 || F % p.rt_per_unit ||
         2 * p.sgu_row > kSlotBytes || p.dn_per_unit < 1 || H % p.R)
         return dfail(TSB_ERR_UNSUPPORTED, "decode: rows do not fit the ring slots");
     int dev = 0, reserved = 0;

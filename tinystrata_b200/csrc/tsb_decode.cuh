@@ -179,39 +179,77 @@ __device__ __forceinline__ int p3_units(const DecParams& p, int ng) {
 }
 
 // -------------------------------------------------------------------------------------------------- producer
+struct BulkCopy {
+    const void* src;
+    uint32_t dst;     // offset in the slot
+    uint32_t bytes;
+};
+
 struct Producer {
-    uint32_t seq = 0;
+    uint32_t seq = 0;   // ring sequence number of the next unit (identical in every lane of the producer warp)
     uint8_t* ring;
     DecShared* S;
     const DecParams* p;
 
-    __device__ bool acquire(uint32_t& slot) {
-        slot = seq % kSlots;
-        if (seq >= (uint32_t) kSlots) {
-            const uint32_t par = ((seq / kSlots) - 1) & 1u;
-            if (!mbar_try_wait(&S->empty[slot], par)) {
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(&S->empty[slot], par)) {
-                    if (globaltimer() - t0 > kWaitNs || S->abort) {
-                        report_detail(p->err, 0x310u, seq, (unsigned) S->prod_state, (unsigned) S->claim, blockIdx.x);
-                        S->abort = 1;
-                        return false;
-                    }
-                }
+    __device__ uint8_t* slot_ptr(uint32_t slot) const { return ring + (size_t) slot * kSlotBytes; }
+    // Is the slot of sequence number s free (its previous lap released by the consumers)?  wait: bounded wait.
+    __device__ bool slot_free(uint32_t s, bool wait) {
+        if (s < (uint32_t) kSlots) return true;
+        const uint32_t slot = s % kSlots, par = ((s / kSlots) - 1) & 1u;
+        if (!wait) return mbar_test_wait(&S->empty[slot], par);
+        if (mbar_try_wait(&S->empty[slot], par)) return true;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(&S->empty[slot], par)) {
+            if (globaltimer() - t0 > kWaitNs || S->abort) {
+                report_detail(p->err, 0x310u, s, (unsigned) S->prod_state, (unsigned) S->claim, blockIdx.x);
+                S->abort = 1;
+                return false;
             }
         }
         return true;
     }
-    __device__ uint8_t* slot_ptr(uint32_t slot) const { return ring + (size_t) slot * kSlotBytes; }
-    // this unit's lap on its slot, published for the consumers (before its bytes are expected)
-    __device__ void start(uint32_t slot) {
-        S->slot_lap[slot] = (int) (seq / kSlots);
-        __threadfence_block();
-    }
-    __device__ void finish(uint32_t slot) {
-        ++seq;
-        S->prod_seq = (int) seq;
-        (void) slot;
+    // Units [lo, hi) of a phase.  copies(u): bulk copies of unit u (<= 32 over a batch); bytes(u): their total;
+    // copy(u, c): copy c of unit u (source, offset in the slot, bytes).  Lane 0 takes the next slot (waiting) and the
+    // free ones after it; lane j starts unit j of the batch (publishes its lap, arms its barrier); then every lane
+    // issues its copy in ONE converged instruction (a cp.async.bulk issued under divergence goes out lane by lane,
+    // each holding the warp for a fraction of a memory latency).
+    template <class NC, class NB, class CP>
+    __device__ bool produce(int lo, int hi, NC copies, NB bytes, CP copy) {
+        const int lane = threadIdx.x & 31;
+        for (int u = lo; u < hi;) {
+            int nb = 0;
+            if (lane == 0 && slot_free(seq, true)) {
+                int ncp = copies(u);
+                nb = 1;
+                while (u + nb < hi && nb < kSlots && ncp + copies(u + nb) <= 32 && slot_free(seq + nb, false))
+                    ncp += copies(u + nb++);
+            }
+            nb = __shfl_sync(0xffffffffu, nb, 0);
+            if (nb == 0) return false;
+            if (lane < nb) {
+                const uint32_t s = seq + lane, slot = s % kSlots;
+                S->slot_lap[slot] = (int) (s / kSlots);
+                mbar_expect_tx(&S->full[slot], bytes(u + lane));
+            }
+            __syncwarp();
+            int mj = -1, mc = 0, base = 0;
+            for (int j = 0; j < nb; ++j) {
+                const int n = copies(u + j);
+                if (lane >= base && lane < base + n) {
+                    mj = j;
+                    mc = lane - base;
+                }
+                base += n;
+            }
+            const BulkCopy cp = copy(u + max(mj, 0), mc);
+            const uint32_t slot = (seq + (uint32_t) max(mj, 0)) % kSlots;
+            if (mj >= 0) bulk_g2s(slot_ptr(slot) + cp.dst, cp.src, cp.bytes, &S->full[slot]);
+            __syncwarp();
+            seq += (uint32_t) nb;
+            u += nb;
+            if (lane == 0) S->prod_seq = (int) seq;
+        }
+        return true;
     }
 };
 
@@ -248,16 +286,15 @@ __device__ __forceinline__ void quantize_rows_to_smem(const float* src, int rows
 }
 
 // A contiguous fp32 array (rows of 32-value blocks; written by other CTAs of this launch, or in shared memory) into
-// q8_1 codes and fp16-rounded scales in shared memory: 8 lanes per block, 4 values each (float4), up to 4 loads in
-// flight per lane before any arithmetic.  The block scale is amax / 127 with the reference's division and the codes
+// q8_1 codes and fp16-rounded scales in shared memory: 8 lanes per block, 4 values each (float4), B loads in flight
+// per lane before any arithmetic.  The block scale is amax / 127 with the reference's division and the codes
 // round(x / d): the same codes and scale as the reference's quantiser, whatever the lane layout (the fp16 sum it also
 // stores is not formed: no format here reads it).
-template <bool FROM_SMEM>
+template <bool FROM_SMEM, int B = FROM_SMEM ? 1 : 2>
 __device__ __forceinline__ void quantize_blocks(const float* src, int n, int8_t* codes, float* dsc, int warp, int lane,
                                                 int nwarps) {
     const int n4 = n / 4;
     const int stride = nwarps * 32;
-    constexpr int B = 4;
     for (int base = warp * 32 + lane; base - lane < n4; base += B * stride) {
         float4 v[B];
 #pragma unroll
@@ -385,104 +422,104 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     __syncthreads();
 
     // ============================================================================================ producer
+    // The whole warp: lane 0 takes free ring slots in order, then the lanes issue the batch's bulk copies side by side
+    // (one thread's cp.async.bulk issues serialise at a memory latency's fraction each; 32 lanes overlap them).
     if (warp == kDecWarps - 1) {
-        if (lane != 0) return;
         Producer pr;
         pr.ring = ring;
         pr.S = &S;
         pr.p = &p;
         for (int l = 0; l < p.n_layers && !S.abort; ++l) {
             const DecLayer L = p.layers[l];
-            S.prod_state = (l << 4) | 1;
-            // P1
+            if (lane == 0) S.prod_state = (l << 4) | 1;
+            // P1: router half rows (one copy), shared gate/up row pairs (two)
             const Range r1 = split(p1_units(p), gridDim.x, blockIdx.x);
-            for (int u = r1.lo; u < r1.hi; ++u) {
-                uint32_t slot;
-                if (!pr.acquire(slot)) break;
-                uint8_t* dst = pr.slot_ptr(slot);
-                if (u < 2 * (p.E + 1)) {
+            const int nrh = 2 * (p.E + 1);
+            auto p1_copies = [&](int u) { return u < nrh ? 1 : 2; };
+            auto p1_bytes = [&](int u) { return u < nrh ? (uint32_t) (p.H / 2 * 4) : 2 * p.sgu_row; };
+            auto p1_copy = [&](int u, int c) -> BulkCopy {
+                if (u < nrh) {
                     const int o = u >> 1, half = u & 1;
-                    const uint32_t nb = (uint32_t) (p.H / 2 * 4);
-                    pr.start(slot); mbar_expect_tx(&S.full[slot], nb);
-                    bulk_g2s(dst, L.router + (size_t) o * p.H + half * (p.H / 2), nb, &S.full[slot]);
-                } else {
-                    const int r = u - 2 * (p.E + 1);
-                    pr.start(slot); mbar_expect_tx(&S.full[slot], 2 * p.sgu_row);
-                    bulk_g2s(dst, L.sh_blob + (size_t) r * p.sgu_row, p.sgu_row, &S.full[slot]);
-                    bulk_g2s(dst + p.sgu_row, L.sh_blob + p.s_up_off + (size_t) r * p.sgu_row, p.sgu_row, &S.full[slot]);
+                    return {L.router + (size_t) o * p.H + half * (p.H / 2), 0u, (uint32_t) (p.H / 2 * 4)};
                 }
-                pr.finish(slot);
-            }
-            stamp(p, l, 9);
-            S.prod_state = (l << 4) | 2;
-            {   // this layer's routing
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(&S.route, (uint32_t) (l & 1))) {
-                    if (globaltimer() - t0 > kWaitNs || S.abort) {
-                        report_error(p.err, 0x320u);
-                        S.abort = 1;
-                        break;
+                const size_t off = (size_t) (u - nrh) * p.sgu_row + (c ? p.s_up_off : 0);
+                return {L.sh_blob + off, c * p.sgu_row, p.sgu_row};
+            };
+            if (!pr.produce(r1.lo, r1.hi, p1_copies, p1_bytes, p1_copy)) break;
+            if (lane == 0) stamp(p, l, 9);
+            if (lane == 0) S.prod_state = (l << 4) | 2;
+            {   // this layer's routing (lane 0 waits; the warp barrier orders the routing tables for the other lanes)
+                int ok = 1;
+                if (lane == 0) {
+                    const uint64_t t0 = globaltimer();
+                    while (!mbar_try_wait(&S.route, (uint32_t) (l & 1))) {
+                        if (globaltimer() - t0 > kWaitNs || S.abort) {
+                            report_error(p.err, 0x320u);
+                            S.abort = 1;
+                            break;
+                        }
                     }
+                    ok = !S.abort;
                 }
-                if (S.abort) break;
+                __syncwarp();
+                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
             }
             const int ng = S.n_groups;
-            stamp(p, l, 10);
-            S.prod_state = (l << 4) | 3 | (ng << 16);
-            // P2
+            if (lane == 0) stamp(p, l, 10);
+            if (lane == 0) S.prod_state = (l << 4) | 3 | (ng << 16);
+            // P2: routed gate/up rows (rt_per_unit consecutive rows of one expert: the gate block, then the up block),
+            // then shared down rows (sd_per_unit consecutive rows, one copy)
             const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
             const Range r2 = split(n2, gridDim.x, blockIdx.x);
-            for (int u = r2.lo; u < r2.hi; ++u) {
-                uint32_t slot;
-                if (!pr.acquire(slot)) break;
-                uint8_t* dst = pr.slot_ptr(slot);
+            auto p2_copies = [&](int u) { return u < nrt ? 2 : 1; };
+            auto p2_bytes = [&](int u) {
+                return u < nrt ? (uint32_t) (min(p.rt_per_unit, ng * p.F - u * p.rt_per_unit) * 2 * p.gu_row)
+                               : (uint32_t) p.sd_per_unit * p.sd_row;
+            };
+            auto p2_copy = [&](int u, int c) -> BulkCopy {
                 if (u < nrt) {
-                    const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * p.F);
-                    pr.start(slot); mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * 2 * p.gu_row);
-                    for (int i = i0; i < i1; ++i) {
-                        const int g = i / p.F, r = i % p.F;
-                        const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + (size_t) r * p.gu_row;
-                        bulk_g2s(dst, b, p.gu_row, &S.full[slot]);
-                        bulk_g2s(dst + p.gu_row, b + p.up_off, p.gu_row, &S.full[slot]);
-                        dst += 2 * p.gu_row;
-                    }
-                } else {
-                    const int r0 = (u - nrt) * p.sd_per_unit;
-                    const uint32_t nb = (uint32_t) p.sd_per_unit * p.sd_row;
-                    pr.start(slot); mbar_expect_tx(&S.full[slot], nb);
-                    bulk_g2s(dst, L.sh_blob + p.s_down_off + (size_t) r0 * p.sd_row, nb, &S.full[slot]);
+                    const int i0 = u * p.rt_per_unit, n = min(p.rt_per_unit, ng * p.F - i0);
+                    const int g = i0 / p.F, r = i0 % p.F;
+                    const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + (size_t) r * p.gu_row;
+                    return {b + (c ? p.up_off : 0), (uint32_t) (c * n) * p.gu_row, (uint32_t) n * p.gu_row};
                 }
-                pr.finish(slot);
-            }
-            stamp(p, l, 11);
-            S.prod_state = (l << 4) | 4 | (ng << 16);
-            // P3
+                const int r0 = (u - nrt) * p.sd_per_unit;
+                return {L.sh_blob + p.s_down_off + (size_t) r0 * p.sd_row, 0u, (uint32_t) p.sd_per_unit * p.sd_row};
+            };
+            if (!pr.produce(r2.lo, r2.hi, p2_copies, p2_bytes, p2_copy)) break;
+            if (lane == 0) stamp(p, l, 11);
+            if (lane == 0) S.prod_state = (l << 4) | 4 | (ng << 16);
+            // P3: this CTA's down rows of each group, task i = (group i / nch, chunk i % nch): a unit's tasks of one
+            // group are consecutive rows, one copy per group it touches
             const Range ch = my_chunks(p);
-            const int ntask = (ch.hi - ch.lo) * ng;
-            const int n3 = p3_units(p, ng);
+            const int nch = ch.hi - ch.lo, ntask = nch * ng;
             const uint32_t cb = (uint32_t) p.R * p.d_row;
-            for (int u = 0; u < n3; ++u) {
-                uint32_t slot;
-                if (!pr.acquire(slot)) break;
-                uint8_t* dst = pr.slot_ptr(slot);
+            auto p3_copies = [&](int u) {
                 const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
-                pr.start(slot); mbar_expect_tx(&S.full[slot], (uint32_t) (i1 - i0) * cb);
-                for (int i = i0; i < i1; ++i) {
-                    const int c = ch.lo + i / ng, g = i % ng;
-                    const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + p.down_off + (size_t) c * cb;
-                    bulk_g2s(dst, b, cb, &S.full[slot]);
-                    dst += cb;
-                }
-                pr.finish(slot);
-            }
-            stamp(p, l, 12);
+                return (i1 - 1) / nch - i0 / nch + 1;
+            };
+            auto p3_bytes = [&](int u) {
+                const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
+                return (uint32_t) (i1 - i0) * cb;
+            };
+            auto p3_copy = [&](int u, int c) -> BulkCopy {
+                const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
+                const int g = i0 / nch + c;
+                const int a0 = max(i0, g * nch), a1 = min(i1, (g + 1) * nch);
+                const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + p.down_off +
+                                   (size_t) (ch.lo + a0 - g * nch) * cb;
+                return {b, (uint32_t) (a0 - i0) * cb, (uint32_t) (a1 - a0) * cb};
+            };
+            if (!pr.produce(0, p3_units(p, ng), p3_copies, p3_bytes, p3_copy)) break;
+            if (lane == 0) stamp(p, l, 12);
         }
         // wind down: every copy issued is complete before the CTA may exit (bounded)
-        for (uint32_t s = pr.seq > kSlots ? pr.seq - kSlots : 0; s < pr.seq; ++s) {
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait(&S.full[s % kSlots], (s / kSlots) & 1u))
-                if (globaltimer() - t0 > kWaitNs) break;
-        }
+        if (lane == 0)
+            for (uint32_t s = pr.seq > kSlots ? pr.seq - kSlots : 0; s < pr.seq; ++s) {
+                const uint64_t t0 = globaltimer();
+                while (!mbar_try_wait(&S.full[s % kSlots], (s / kSlots) & 1u))
+                    if (globaltimer() - t0 > kWaitNs) break;
+            }
         return;
     }
 
@@ -658,15 +695,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     const uint8_t* gate = buf;
                     const uint8_t* up = buf + p.sgu_row;
                     for (int t = 0; t < T; ++t) {
-                        typename Fmt<T_Q8_0>::Act a[1][8];
+                        // row_dot's order (lane + 32 j, j ascending, then the xor tree), one activation at a time
                         auto src = [&](int blk) { return xv.block(t, blk); };
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if (lane + 32 * j < Cs) a[0][j] = Fmt<T_Q8_0>::act(src, lane + 32 * j);
-                        float sg[1], su[1];
-                        row_dot<T_Q8_0, 8, 1>(gate, Cs, lane, a, 1, itab, sg);
-                        row_dot<T_Q8_0, 8, 1>(up, Cs, lane, a, 1, itab, su);
-                        if (lane == 0) p.hsh[(size_t) t * p.FS + r] = act_value(ACT_SWIGLU, sg[0], su[0], INFINITY);
+                        float sg = 0.0f, su = 0.0f;
+#pragma unroll 2
+                        for (int k = lane; k < Cs; k += 32) {
+                            const typename Fmt<T_Q8_0>::Act a = Fmt<T_Q8_0>::act(src, k);
+                            sg += Fmt<T_Q8_0>::apply(decode_call<T_Q8_0>(gate, k, itab), a);
+                            su += Fmt<T_Q8_0>::apply(decode_call<T_Q8_0>(up, k, itab), a);
+                        }
+                        sg = warp_sum(sg);
+                        su = warp_sum(su);
+                        if (lane == 0) p.hsh[(size_t) t * p.FS + r] = act_value(ACT_SWIGLU, sg, su, INFINITY);
                     }
                 }
                 release(s);
@@ -798,10 +838,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 const int u = r2.lo + k;
                 if (u < nrt) {
                     const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * F);
-                    for (int i = i0; i < i1; ++i) {
+                    for (int i = i0; i < i1; ++i) {   // the unit's gate rows, then its up rows
                         const int g = i / F, r = i % F;
-                        const uint8_t* gate = buf + (size_t) (i - i0) * 2 * p.gu_row;
-                        const uint8_t* up = gate + p.gu_row;
+                        const uint8_t* gate = buf + (size_t) (i - i0) * p.gu_row;
+                        const uint8_t* up = gate + (size_t) (i1 - i0) * p.gu_row;
                         const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
                         for (int eb = e0; eb < e1; ++eb) {   // decode groups rarely hold more than one entry
                             const int tok = S.ent_tok[eb];
@@ -848,7 +888,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
             quantize_blocks<false>(p.hbuf, T * K * F, hq_codes, hq_d, warp, lane, kDecConsumers);
             named_sync(1, kDecCThreads);
             const Range ch = my_chunks(p);
-            const int ntask = (ch.hi - ch.lo) * ng;
+            const int nch = ch.hi - ch.lo, ntask = nch * ng;
             const int mine = p3_units(p, ng);
             int k;
             while (claim(mine, k)) {
@@ -857,7 +897,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 const uint8_t* buf = ring + (size_t) (s % kSlots) * kSlotBytes;
                 const int i0 = k * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
                 for (int i = i0; i < i1; ++i) {
-                    const int cl = i / ng, g = i % ng;   // chunk index within this CTA, group
+                    const int cl = i % nch, g = i / nch;   // chunk index within this CTA, group (group-major tasks)
                     const uint8_t* rows = buf + (size_t) (i - i0) * p.R * p.d_row;
                     const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
                     for (int eb = e0; eb < e1; ++eb) {
