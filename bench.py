@@ -25,6 +25,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_LAYERS = 40   # --layers changes it for profiling captures only (a smaller device footprint); the bench is 40
+# DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch
+# (profiles/k_decode_layers_qwen_decode_T1_4layers_full.md: 64.19 MB per launch); traffic grows with the layer count,
+# so a launch of N layers moves N times this.
+TRAFFIC_PER_LAYER_T1 = 64.19e6 / 4
 METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
 
 
@@ -331,7 +335,11 @@ def main():
             "fused_vs_layerwise": {"max_abs_over_rms": rel, "same_routing": same_routing},
             "roofline": {"bound": "hbm", "kernel": "k_decode_layers (fused decode step, 40 layers)",
                          "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
-                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": k_bytes,
+                         "peak_kind": peak_kind,
+                         "traffic": TRAFFIC_PER_LAYER_T1 * N_LAYERS if T == 1 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4-layer capture scaled "
+                                           "to the launch's layers" if T == 1 else None,
+                         "algorithmic_bytes_per_launch": k_bytes,
                          "avg_launch_ms": k_avg_ms, "layer_algorithmic_bytes": alg_bytes_per_layer},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
