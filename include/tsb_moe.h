@@ -106,6 +106,19 @@ int tsb_native_expert_grouped_act(const tsb_expert_layout* L, const uint64_t* gr
                                   int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, void* scratch,
                                   float* out, int act, float limit, void* stream);
 
+/* tsb_native_expert_grouped (SwiGLU) without a caller scratch buffer: the hidden vectors live in a fixed 1 MiB device
+ * array inside this library (cap_entries * n_ff * 4 bytes, rounded up to 256, must fit: 128 entries at n_ff 2048;
+ * larger calls return TSB_ERR_WORKSPACE and launch nothing).  For callers that hold no workspace and must not
+ * allocate one on the call path.  The array and the call's bounded-wait error word start at zero when the module loads;
+ * the hidden vectors need no clearing between calls.  There is ONE array per device: calls that overlap in time on a
+ * device (other streams or threads) race on it.  Its address is looked up once per device with cudaGetSymbolAddress
+ * at the first call, which may load the module: make that first call outside any stream capture.  No counterpart in
+ * the reference (native_expert_grouped, iq_kernels.hpp:75-78, always takes the caller's scratch). */
+int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                                      const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                                      int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, float* out,
+                                      void* stream);
+
 /* Bench only: 0 = both expert kernels (default), 1 = gate/up + activation only, 2 = down only (reads the scratch the
  * previous call left).  Replaces native_expert_set_mode's phase argument (iq_kernels.hpp:85).  Process-wide; set
  * outside graph capture. */

@@ -65,6 +65,8 @@ SIGNATURES = {
                                             _i64]),
     "tsb_native_expert_grouped_act": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
                                                 C.c_int, _f, _p]),
+    "tsb_native_expert_grouped_noalloc": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
+                                                    _p]),
     "tsb_moe_combine": (C.c_int, [_p, _p, _p, _p, C.c_int, _p, _p, C.c_int, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
     "tsb_moe_sum": (C.c_int, [_p, _p, _p, C.c_int, C.c_int, C.c_int, _p]),
     "tsb_rms_norm_q8_1": (C.c_int, [_p, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
@@ -216,6 +218,17 @@ def native_expert_grouped(L: ExpertLayout, groups: Groups, cap_groups: int, cap_
         _check(lib().tsb_native_expert_grouped(*args, _stream(stream), 0), "native_expert_grouped")
     else:
         _check(lib().tsb_native_expert_grouped_act(*args, act, limit, _stream(stream)), "native_expert_grouped_act")
+    return out
+
+
+def native_expert_grouped_noalloc(L: ExpertLayout, groups: Groups, cap_groups: int, cap_entries: int, x_q8_1, out,
+                                  stream=None):
+    """native_expert_grouped (SwiGLU) with the library's fixed 1 MiB device scratch instead of a caller buffer; one
+    copy per device, so calls must not overlap in time."""
+    _check(lib().tsb_native_expert_grouped_noalloc(C.byref(L), _ptr(groups.grp_ptr), _ptr(groups.grp_start),
+                                                   _ptr(groups.n_groups), _ptr(groups.ent_dst), _ptr(groups.ent_tok),
+                                                   cap_groups, cap_entries, _ptr(x_q8_1), _ptr(out), _stream(stream)),
+           "native_expert_grouped_noalloc")
     return out
 
 

@@ -737,6 +737,84 @@ int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, i
     return cuda_status("moe_sum");
 }
 
+// ------------------------------------------------------------------------------------ no-allocation grouped experts
+// tsb_native_expert_grouped with its scratch (the entries' hidden vectors, fp32 [cap_entries][n_ff]) in a fixed
+// device array of this library instead of a caller buffer, and a bounded-wait error word of its own.  Both are
+// zero-initialised when the module loads; the hidden vectors need no clearing (the gate/up kernel writes every entry
+// the down kernel then reads), and the error word is only ever set (a wait that gave up), never cleared here.
+// One copy per device: two calls in flight at the same time on one device (other streams, other threads) race on it.
+static constexpr size_t kNoAllocScratchBytes = (size_t) 1 << 20;   // 1 MiB: 128 entries x n_ff 2048 fp32
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) unsigned g_noalloc_err;
+
+struct NoAllocDev {
+    bool ready = false;
+    int sms = 0;
+    void* scratch = nullptr;
+    unsigned* err = nullptr;
+};
+static NoAllocDev g_noalloc[64];
+static std::mutex g_noalloc_mu;
+
+// The current device's addresses of the fixed arrays, looked up once per device (cudaGetSymbolAddress; the first
+// call may load the module, so it is made outside any stream capture).
+static int noalloc_dev(NoAllocDev*& out) {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) {
+        cudaGetLastError();
+        return fail(TSB_ERR_CUDA, "native_expert_grouped_noalloc: no CUDA device");
+    }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDev& N = g_noalloc[d];
+    if (!N.ready) {
+        cudaError_t e = cudaDeviceGetAttribute(&N.sms, cudaDevAttrMultiProcessorCount, d);
+        void* sp = nullptr;
+        void* ep = nullptr;
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&sp, g_noalloc_scratch);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&ep, g_noalloc_err);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(TSB_ERR_CUDA, "native_expert_grouped_noalloc: device %d: %s", d, cudaGetErrorString(e));
+        }
+        N.scratch = sp;
+        N.err = (unsigned*) ep;
+        N.ready = true;
+    }
+    out = &N;
+    return TSB_OK;
+}
+
+int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
+                                      const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
+                                      int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, float* out,
+                                      void* stream) {
+    if (cap_groups <= 0 || cap_entries <= 0) return TSB_OK;
+    if (!L || !grp_ptr || !grp_start || !n_groups || !ent_dst || !ent_tok || !x_q8_1 || !out)
+        return fail(TSB_ERR_ARG, "native_expert_grouped_noalloc: null argument");
+    if (!tsb_native_expert_supported(L->gu_type, L->d_type, L->n_embd, L->n_ff))
+        return fail(TSB_ERR_UNSUPPORTED, "native_expert_grouped_noalloc: types %d/%d at %lld/%lld", L->gu_type,
+                    L->d_type, (long long) L->n_embd, (long long) L->n_ff);
+    if (L->up_off % 16 || L->down_off % 16 || L->bytes % 16)
+        return fail(TSB_ERR_ALIGN, "native_expert_grouped_noalloc: blob offsets must be multiples of 16 bytes");
+    const uint64_t need = tsb_native_expert_scratch_bytes(cap_entries, L->n_ff);
+    if (need > kNoAllocScratchBytes)
+        return fail(TSB_ERR_WORKSPACE,
+                    "native_expert_grouped_noalloc: %lld entries x n_ff %lld need %llu bytes of scratch, more than the "
+                    "fixed %zu; use tsb_native_expert_grouped with a caller buffer",
+                    (long long) cap_entries, (long long) L->n_ff, (unsigned long long) need, kNoAllocScratchBytes);
+    NoAllocDev* N = nullptr;
+    const int rc = noalloc_dev(N);
+    if (rc != TSB_OK) return rc;
+    DevInfo di;
+    di.sms = N->sms;
+    di.err = N->err;
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    float* h = (float*) N->scratch;
+    const int r1 = gu_dispatch(L, g, cap_groups, x_q8_1, h, ACT_SWIGLU, INFINITY, cs(stream), &di);
+    if (r1 != TSB_OK) return r1;
+    return down_dispatch(L, g, cap_groups, h, out, cs(stream), &di);
+}
+
 int tsb_debug_row_calls(int ggml_type, const void* row, const void* x_q8_1, int64_t n, int32_t* sumi, float* val,
                         void* stream) {
     const int64_t rb = tsb_row_bytes(ggml_type, n);
