@@ -88,6 +88,12 @@ int tsb_moe_group(const int32_t* ids, int n_ent, int K, int n_expert, const void
                   uint64_t* grp_ptr, int32_t* grp_start, int32_t* n_groups, int32_t* ent_dst, int32_t* ent_tok,
                   void* stream);
 
+/* Prefill permutation: entries e = t * K + k (ids [n_ent]) sorted stably by expert.  bounds[x] = first row of expert
+ * x (bounds[n_expert] = entries placed), row_ent[row] = e, row_tok[row] = e / K, rinv[e] = row (-1 for an id outside
+ * [0, n_expert), which is dropped).  Replaces k_route_count / k_route_scan / k_route_scatter
+ * (src/qwen35/q36_engine.cu:486-510) without their device-to-host copy: the bounds stay on the device. */
+int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t* bounds, int32_t* row_ent,
+                     int32_t* row_tok, int32_t* rinv, void* stream);
 /* --------------------------------------------------------------------------------------------- experts */
 /* Grouped experts, SwiGLU: for each group g (blob grp_ptr[g]) and entry e in [grp_start[g], grp_start[g+1]):
  * out[ent_dst[e]] = down(q8_1(silu(gate . x) * (up . x))) with x = token ent_tok[e] of x_q8_1 (n_embd / 32 blocks per
@@ -118,6 +124,21 @@ int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t
                                       const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
                                       int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, float* out,
                                       void* stream);
+
+/* Prefill grouped gate/up on the tensor cores: for group g (rows [bounds[g], bounds[g+1]), weights blobs + g *
+ * blob_stride in layout L; bounds null: one group of n_rows rows), h[row] = q8_1(act(gate . x, up . x)) with x the
+ * q8_1 row row_tok ? row_tok[row] : row of x_q8_1 (n_embd / 32 blocks per row, as quantize_q8_1_rows writes it);
+ * h_q8_1 holds n_rows x n_ff / 32 blocks.  The block dots are exact and scaled and summed in fp32 block after block,
+ * as the reference's.  act as tsb_native_expert_grouped_act.  Q4_0 weights with block scales |d| <= 8; n_embd and
+ * n_ff multiples of 64, at least 128.  Replaces the gate/up mmq::Context::run + mmq::swiglu + the re-quantisation of
+ * the prompt path (src/prefill/moe_mmq.cu:334-384, 123-131). */
+int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                       int n_groups, int n_rows, const void* x_q8_1, const int32_t* row_tok, void* h_q8_1, int act,
+                       float limit, void* stream);
+/* Prefill grouped down: out[row] = down . h[row] (fp32 [n_rows][n_embd], 16-byte aligned) with the groups as above
+ * and h the q8_1 rows tsb_moe_prefill_gu wrote.  Replaces the down mmq::Context::run (src/prefill/moe_mmq.cu:334-384). */
+int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                         int n_groups, int n_rows, const void* h_q8_1, float* out, void* stream);
 
 /* Bench only: 0 = both expert kernels (default), 1 = gate/up + activation only, 2 = down only (reads the scratch the
  * previous call left).  Replaces native_expert_set_mode's phase argument (iq_kernels.hpp:85).  Process-wide; set

@@ -65,6 +65,10 @@ SIGNATURES = {
                                             _i64]),
     "tsb_native_expert_grouped_act": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
                                                 C.c_int, _f, _p]),
+    "tsb_moe_dispatch": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, _p, _p, _p, _p, _p]),
+    "tsb_moe_prefill_gu": (C.c_int, [C.POINTER(ExpertLayout), _p, _u64, _p, C.c_int, C.c_int, _p, _p, _p, C.c_int, _f,
+                                     _p]),
+    "tsb_moe_prefill_down": (C.c_int, [C.POINTER(ExpertLayout), _p, _u64, _p, C.c_int, C.c_int, _p, _p, _p]),
     "tsb_native_expert_grouped_noalloc": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                                     _p]),
     "tsb_moe_combine": (C.c_int, [_p, _p, _p, _p, C.c_int, _p, _p, C.c_int, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
@@ -229,6 +233,46 @@ def native_expert_grouped_noalloc(L: ExpertLayout, groups: Groups, cap_groups: i
                                                    _ptr(groups.n_groups), _ptr(groups.ent_dst), _ptr(groups.ent_tok),
                                                    cap_groups, cap_entries, _ptr(x_q8_1), _ptr(out), _stream(stream)),
            "native_expert_grouped_noalloc")
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ prefill
+def moe_dispatch(ids, n_expert: int, stream=None):
+    """Stable sort of the entries by expert (q36_engine.cu:486-510): (bounds [E+1], row_ent, row_tok, rinv)."""
+    import torch
+    T, K = ids.shape
+    n = T * K
+    dev = ids.device
+    bounds = torch.empty(n_expert + 1, dtype=torch.int32, device=dev)
+    row_ent = torch.empty(n, dtype=torch.int32, device=dev)
+    row_tok = torch.empty(n, dtype=torch.int32, device=dev)
+    rinv = torch.empty(n, dtype=torch.int32, device=dev)
+    _check(lib().tsb_moe_dispatch(_ptr(ids), n, K, n_expert, _ptr(bounds), _ptr(row_ent), _ptr(row_tok), _ptr(rinv),
+                                  _stream(stream)), "moe_dispatch")
+    return bounds, row_ent, row_tok, rinv
+
+
+def moe_prefill_gu(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, x_q8_1, row_tok=None,
+                   act: int = ACT_SWIGLU, limit: float = float("inf"), h=None, stream=None):
+    """Grouped gate/up + activation on the tensor cores: x_q8_1 (quantize_q8_1_rows's blocks) -> the hidden vectors'
+    q8_1 blocks uint8 [n_rows, n_ff / 32 * 36]."""
+    import torch
+    if h is None:
+        h = torch.empty((n_rows, L.n_ff // 32 * Q8_1_BYTES), dtype=torch.uint8, device=x_q8_1.device)
+    _check(lib().tsb_moe_prefill_gu(C.byref(L), _ptr(blobs), blob_stride, _ptr(bounds), n_groups, n_rows,
+                                    _ptr(x_q8_1), _ptr(row_tok), _ptr(h), act, limit, _stream(stream)),
+           "moe_prefill_gu")
+    return h
+
+
+def moe_prefill_down(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, h_q8_1, out=None,
+                     stream=None):
+    """Grouped down on the tensor cores: moe_prefill_gu's q8_1 rows -> fp32 [n_rows, n_embd]."""
+    import torch
+    if out is None:
+        out = torch.empty((n_rows, L.n_embd), dtype=torch.float32, device=h_q8_1.device)
+    _check(lib().tsb_moe_prefill_down(C.byref(L), _ptr(blobs), blob_stride, _ptr(bounds), n_groups, n_rows,
+                                      _ptr(h_q8_1), _ptr(out), _stream(stream)), "moe_prefill_down")
     return out
 
 

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsb_moe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["tsb_moe.cu", "tsb_decode.cu", "tsb_prefill.cu"]
+SOURCES = ["tsb_moe.cu", "tsb_decode.cu"]
 HEADERS = ["tsb_device.cuh", "tsb_formats.cuh", "tsb_kernels.cuh", "tsb_decode.cuh", "tsb_prefill.cuh", "codebooks.inc",
            "../../include/tsb_moe.h"]
 FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",

@@ -129,9 +129,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // Consumers: all 480 threads.  Thread 0 publishes this CTA's arrival and waits for the others (acquire), bounded.
 __device__ bool grid_barrier(const DecParams& p, DecShared& S, unsigned& target, unsigned site) {

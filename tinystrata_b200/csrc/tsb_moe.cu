@@ -1,6 +1,7 @@
 // tsb_moe.cu - the B200 MoE expert path behind TinyStrata's expert-layer entry points: q8_1 quantiser, router GEMV,
 // softmax / sigmoid top-k routers, decode grouping, grouped expert GEMVs, combine.  The C ABI is include/tsb_moe.h.
 #include "tsb_kernels.cuh"
+#include "tsb_prefill.cuh"
 #include "../../include/tsb_moe.h"
 
 #include <cuda_runtime.h>
@@ -735,6 +736,95 @@ int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, i
     if (!x || !w || !acc || n <= 0 || n_used < 1) return fail(TSB_ERR_ARG, "moe_sum: arguments");
     k_moe_sum<<<dim3((unsigned) ((n + 255) / 256), (unsigned) rows), 256, 0, cs(stream)>>>(x, w, acc, n, n_used);
     return cuda_status("moe_sum");
+}
+
+// ------------------------------------------------------------------------------------------------ prefill
+int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t* bounds, int32_t* row_ent,
+                     int32_t* row_tok, int32_t* rinv, void* stream) {
+    if (n_ent < 0 || K < 1 || n_expert < 1 || n_expert > 1024 || !bounds)
+        return fail(TSB_ERR_ARG, "moe_dispatch: arguments");
+    if (n_ent > 0 && (!ids || !row_ent || !row_tok || !rinv)) return fail(TSB_ERR_ARG, "moe_dispatch: null argument");
+    k_dispatch_count<<<1, 1024, 0, cs(stream)>>>(ids, n_ent, n_expert, bounds, rinv);
+    if (n_ent > 0) k_dispatch_scatter<<<n_expert, 1024, 0, cs(stream)>>>(ids, n_ent, K, bounds, row_ent, row_tok, rinv);
+    return cuda_status("moe_dispatch");
+}
+
+static int pf_launch(int mode, PfParams& pp, cudaStream_t s) {
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    pp.err = di->err;
+    auto kern = mode == PF_GU ? k_pf_gemm<PF_GU> : k_pf_gemm<PF_DOWN>;
+    static bool attr[2] = {false, false};
+    if (!attr[mode]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPfSmem) != cudaSuccess)
+            return cuda_status("prefill: shared memory");
+        attr[mode] = true;
+    }
+    kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
+    return cuda_status(mode == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
+}
+
+static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, int n_groups, int n_rows,
+                    int mode) {
+    if (!L || !blobs || n_rows < 0 || n_groups < 1 || n_groups > kPfMaxGroups)
+        return fail(TSB_ERR_ARG, "moe_prefill: arguments");
+    const int t = mode == PF_GU ? L->gu_type : L->d_type;
+    if (t != T_Q4_0) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0 only)", t);
+    if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 128)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd and n_ff multiples of 64, at least 128");
+    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || L->gu_row % 2 || L->d_row % 2)
+        return fail(TSB_ERR_ALIGN, "moe_prefill: blob alignment");
+    return TSB_OK;
+}
+
+int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                       int n_groups, int n_rows, const void* x_q8_1, const int32_t* row_tok, void* h_q8_1, int act,
+                       float limit, void* stream) {
+    int rc = pf_check(L, blobs, blob_stride, n_groups, n_rows, PF_GU);
+    if (rc != TSB_OK) return rc;
+    if (n_rows == 0) return TSB_OK;
+    if (!x_q8_1 || !h_q8_1 || act < 0 || act > 2 || (bounds == nullptr && n_groups != 1))
+        return fail(TSB_ERR_ARG, "moe_prefill_gu: arguments");
+    if ((uintptr_t) x_q8_1 % 4 || (uintptr_t) h_q8_1 % 4) return fail(TSB_ERR_ALIGN, "moe_prefill_gu: q8_1 alignment");
+    PfParams pp{};
+    pp.bounds = bounds;
+    pp.n_groups = n_groups;
+    pp.n_rows = n_rows;
+    pp.blobs = (const uint8_t*) blobs;
+    pp.blob_stride = blob_stride;
+    pp.w_off = 0;
+    pp.up_off = L->up_off;
+    pp.w_row = (uint32_t) L->gu_row;
+    pp.K = (int) L->n_embd;
+    pp.N = (int) L->n_ff;
+    pp.X = (const BlockQ8_1*) x_q8_1;
+    pp.row_tok = row_tok;
+    pp.Hq = (BlockQ8_1*) h_q8_1;
+    pp.act = act;
+    pp.limit = limit;
+    return pf_launch(PF_GU, pp, cs(stream));
+}
+
+int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                         int n_groups, int n_rows, const void* h_q8_1, float* out, void* stream) {
+    int rc = pf_check(L, blobs, blob_stride, n_groups, n_rows, PF_DOWN);
+    if (rc != TSB_OK) return rc;
+    if (n_rows == 0) return TSB_OK;
+    if (!h_q8_1 || !out || (bounds == nullptr && n_groups != 1)) return fail(TSB_ERR_ARG, "moe_prefill_down: arguments");
+    if ((uintptr_t) h_q8_1 % 4 || (uintptr_t) out % 16) return fail(TSB_ERR_ALIGN, "moe_prefill_down: alignment");
+    PfParams pp{};
+    pp.bounds = bounds;
+    pp.n_groups = n_groups;
+    pp.n_rows = n_rows;
+    pp.blobs = (const uint8_t*) blobs;
+    pp.blob_stride = blob_stride;
+    pp.w_off = L->down_off;
+    pp.w_row = (uint32_t) L->d_row;
+    pp.K = (int) L->n_ff;
+    pp.N = (int) L->n_embd;
+    pp.X = (const BlockQ8_1*) h_q8_1;
+    pp.D = out;
+    return pf_launch(PF_DOWN, pp, cs(stream));
 }
 
 // ------------------------------------------------------------------------------------ no-allocation grouped experts

@@ -1,0 +1,505 @@
+// tsb_prefill.cuh - the prefill (many-token) expert path: dispatch into expert-contiguous rows and the grouped expert
+// products on the 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
+//
+// Reference: the prompt path runs llama.cpp's MMQ over rows sorted by expert (src/prefill/moe_mmq.cu:334-384,
+// moe_mmq.hpp:58-81; permutation q36_engine.cu:486-510; SwiGLU moe_mmq.cu:123-131): per 32-value block an exact
+// integer dot of the q8_1 activation codes with the weight codes, scaled by both blocks' scales and summed in fp32.
+// The same arithmetic here, on tcgen05:
+//   * per 32-value block the tensor core forms S = sum_k q_x[k] * (d_w * (q_w[k] - 8)) exactly: the activation codes
+//     are exact in fp16 and the weight values d_w (q_w - 8) (15 significant bits) are split into fp16 hi + lo parts
+//     (exact), so two fp16 MMAs per 16 values accumulate integers times exact weights over just 32 terms;
+//   * the epilogue warps then add S * d_x (the activation block's scale) into an fp32 accumulator, block after block,
+//     with round-to-nearest FMAs, as the reference's scale-and-sum does.
+// The hidden vector between the products is re-quantised to q8_1 as the reference's quantiser does, so it is the
+// reference's but for values within fp32 rounding of a code boundary.  Weight values are scaled by 2^10 before the
+// split (exact; undone in the epilogue) so that the lo parts of small weights stay out of fp16's subnormal range
+// (|d_w| <= 8 keeps 8 |d_w| 2^10 below fp16's maximum).
+//
+// Kernel shape (one CTA per SM, persistent over output tiles of 128 rows x 128 columns):
+//   warps 0-7   producers: per ring stage (64 values of K) 128 activation rows (two q8_1 blocks each -> fp16 codes)
+//               and 128 weight rows (two Q4_0 blocks -> fp16 hi and lo), in the tensor core's K-major 128-byte
+//               swizzled layout;
+//   warp 8      tensor-memory allocation and the MMA issue (one thread): per 32-value block 4 x tcgen05.mma M128 N128
+//               K16 into one of three block-sum buffers; tcgen05.commit hands the buffer to the epilogue and, every
+//               second block, frees the ring stage;
+//   warps 9-12  epilogue: per block, tcgen05.ld of the block sums and one FMA with the row's activation scale into
+//               the tensor-memory accumulator (tcgen05.ld / tcgen05.st); at the end of the tile the activation and the
+//               q8_1 quantisation (gate/up) or the fp32 store (down).
+// Gate/up tiles interleave the matrices: B rows 0..63 are gate rows j0..j0+63, rows 64..127 the up rows, so one
+// thread holds the gate and up sums of the same 64 hidden values.
+#pragma once
+
+#include "tsb_kernels.cuh"
+
+#include <cuda_fp16.h>
+
+namespace tsb {
+
+constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 4, kPfSBuf = 3;
+constexpr int kPfProducerWarps = 8, kPfMmaWarp = 8, kPfWarps = 13;
+constexpr int kPfThreads = kPfWarps * 32;
+constexpr uint32_t kPfTileA = kPfBM * kPfBK * 2, kPfTileB = kPfBN * kPfBK * 2;   // 16 KB each
+constexpr uint32_t kPfStage = kPfTileA + 2 * kPfTileB;                          // A | B_hi | B_lo
+constexpr uint32_t kPfSmem = kPfStages * kPfStage + 1024;   // + slack (swizzled tiles sit on 1 KB)
+constexpr int kPfMaxGroups = 512;
+constexpr uint32_t kPfAccCol = kPfSBuf * kPfBN;             // TMEM columns: 3 block-sum buffers, then the accumulator
+// instruction descriptor: D f32, A f16, B f16, both K-major, N = 128, M = 128
+constexpr uint32_t kPfIdesc = (1u << 4) | ((uint32_t) (kPfBN >> 3) << 17) | ((uint32_t) (kPfBM >> 4) << 24);
+constexpr float kPfWScale = 1024.0f, kPfWUnscale = 1.0f / 1024.0f;
+
+enum : int { PF_GU = 0, PF_DOWN = 1 };
+
+struct PfParams {
+    // groups: group g owns output rows [bounds[g], bounds[g+1]) and the weight matrix of blob blobs + g * blob_stride
+    const int32_t* bounds;     // [n_groups + 1] on the device (null: one group of n_rows rows)
+    int n_groups;
+    int n_rows;
+    const uint8_t* blobs;
+    uint64_t blob_stride;
+    uint64_t w_off;            // byte offset of the matrix in the blob (gate rows; down rows)
+    uint64_t up_off;           // gate/up: offset of the up rows from the gate rows
+    uint32_t w_row;            // bytes per weight row
+    int K;                     // contraction length (a multiple of 64)
+    int N;                     // output columns (gate/up: n_ff hidden values; down: n_embd)
+    const BlockQ8_1* X;        // activations: row r reads q8_1 row a_row(r) (K / 32 blocks)
+    const int32_t* row_tok;    // a_row(r) = row_tok[r] (null -> r)
+    BlockQ8_1* Hq;             // gate/up output: q8_1 of the hidden vectors [n_rows][N / 32]
+    float* D;                  // down output: fp32 [n_rows][N]
+    int act;
+    float limit;
+    unsigned* err;
+};
+
+// ------------------------------------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint64_t pf_sdesc(uint32_t addr) {   // K-major, 128-byte swizzle, 8-row groups 1 KB apart
+    return (uint64_t) ((addr >> 4) & 0x3FFFu) | ((uint64_t) 1 << 16) | ((uint64_t) (1024 >> 4) << 32) |
+           ((uint64_t) 1 << 46) | ((uint64_t) 2 << 61);
+}
+__device__ __forceinline__ void pf_mma(uint32_t tmem, uint64_t da, uint64_t db, uint32_t acc) {
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+                 ::"r"(tmem), "l"(da), "l"(db), "r"(kPfIdesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void pf_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+                   "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+                   "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                   "=r"(r[30]), "=r"(r[31])
+                 : "r"(addr));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const float (&v)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                 "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+                 ::"r"(addr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                   "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                   "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+                   "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+                   "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+                   "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+                   "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+                   "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+                   "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+                   "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+                   "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// byte offset of the 16-byte chunk c (values 8c..8c+7) of row r inside a K-major 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return (uint32_t) ((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// ------------------------------------------------------------------------------------------------ operand staging
+// One q8_1 block (fp16 d, fp16 sum, 32 int8 codes) -> its codes as fp16 (exact) into chunks 4h..4h+3 of row r:
+// the byte c + 128 under the exponent of 1024 is the fp16 1024 + c + 128, and an exact subtraction of 1152 leaves c.
+__device__ __forceinline__ void stage_q8_codes(const BlockQ8_1* b, uint8_t* tile, int r, int h) {
+    const uint32_t* w = (const uint32_t*) b->qs;
+    const half2 bias = __float2half2_rn(1152.0f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {   // 8 codes: words 2c, 2c+1
+        const uint32_t w0 = __ldg(w + 2 * c) ^ 0x80808080u, w1 = __ldg(w + 2 * c + 1) ^ 0x80808080u;
+        uint32_t out[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {   // codes 2p, 2p+1 of the chunk
+            const uint32_t bits = __byte_perm(p < 2 ? w0 : w1, 0x64646464u, (p & 1) ? 0x4342u : 0x4140u);
+            const half2 v = __hsub2(*(const half2*) &bits, bias);
+            out[p] = *(const uint32_t*) &v;
+        }
+        *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(out[0], out[1], out[2], out[3]);
+    }
+}
+
+// One Q4_0 block (18 bytes at src: fp16 d, 16 bytes of nibbles; 2-byte aligned) of row r -> chunks 4h..4h+3 of the hi
+// and lo tiles: w = d 2^10 (q - 8) (exact in fp32), hi = fp16(w), lo = fp16(w - hi).  Values 0..15 of a block are the
+// low nibbles of bytes 0..15, values 16..31 the high nibbles.
+__device__ __forceinline__ void stage_q4_0(const uint8_t* src, uint8_t* hi_tile, uint8_t* lo_tile, int r, int h) {
+    const uint16_t* s16 = (const uint16_t*) src;
+    const float d = __half2float(__ushort_as_half(__ldg(s16))) * kPfWScale;
+    uint32_t qs[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qs[i] = (uint32_t) __ldg(s16 + 1 + 2 * i) | ((uint32_t) __ldg(s16 + 2 + 2 * i) << 16);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {   // chunk c: values 8c..8c+7 (c < 2 low nibbles, c >= 2 high nibbles)
+        const uint32_t q0 = qs[(c & 1) * 2], q1 = qs[(c & 1) * 2 + 1];
+        const int sh = (c >> 1) * 4;
+        uint32_t oh[4], ol[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t src8 = p < 2 ? q0 : q1;
+            const int byte = (p & 1) * 2;
+            const float v0 = d * (float) ((int) ((src8 >> (8 * byte + sh)) & 0xF) - 8);
+            const float v1 = d * (float) ((int) ((src8 >> (8 * (byte + 1) + sh)) & 0xF) - 8);
+            const half2 vh = __floats2half2_rn(v0, v1);
+            const float2 vhf = __half22float2(vh);
+            const half2 vl = __floats2half2_rn(v0 - vhf.x, v1 - vhf.y);
+            oh[p] = *(const uint32_t*) &vh;
+            ol[p] = *(const uint32_t*) &vl;
+        }
+        *(uint4*) (hi_tile + sw128(r, 4 * h + c)) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+        *(uint4*) (lo_tile + sw128(r, 4 * h + c)) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+    }
+}
+__device__ __forceinline__ void stage_zero(uint8_t* tile, int r, int h) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(0, 0, 0, 0);
+}
+
+// ------------------------------------------------------------------------------------------------ the kernel
+template <int MODE>
+__global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
+    extern __shared__ __align__(1024) uint8_t pf_raw[];
+    uint8_t* smem = (uint8_t*) (((uintptr_t) pf_raw + 1023) & ~(uintptr_t) 1023);
+    __shared__ uint64_t full[kPfStages], empty[kPfStages], s_full[kPfSBuf], s_empty[kPfSBuf];
+    __shared__ uint32_t tbase;
+    __shared__ volatile int abort_flag;
+    __shared__ int32_t gstart[kPfMaxGroups + 1];   // row starts
+    __shared__ int32_t gtile[kPfMaxGroups + 1];    // prefix of 128-row tiles
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = p.n_groups;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPfStages; ++s) {
+            mbar_init(&full[s], kPfProducerWarps);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < kPfSBuf; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], 4);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 32) {
+        int t = 0;
+        for (int g = 0; g <= G; ++g) {
+            const int s = p.bounds ? __ldg(p.bounds + g) : (g == 0 ? 0 : p.n_rows);
+            gstart[g] = s;
+            gtile[g] = t;
+            if (g < G) {
+                const int e = p.bounds ? __ldg(p.bounds + g + 1) : p.n_rows;
+                t += (max(e - s, 0) + kPfBM - 1) / kPfBM;
+            }
+        }
+    }
+    if (warp == kPfMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tbase)), "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tbase;
+    const int n_mt = gtile[G];
+    const int per_tile = MODE == PF_GU ? 64 : kPfBN;   // hidden values (gate/up) or output columns per tile
+    const int n_nt = (p.N + per_tile - 1) / per_tile;
+    const int n_tiles = n_mt * n_nt;
+    const int nb = p.K / 32;            // 32-value blocks of K
+    const int nks = p.K / kPfBK;        // ring stages per tile
+    auto tile_of = [&](int t, int& g, int& row0, int& row1, int& n0) {
+        const int mt = t / n_nt, nt = t % n_nt;
+        int lo = 0, hi = G - 1;
+        while (lo < hi) {   // last group with gtile[g] <= mt (empty groups share their successor's start)
+            const int mid = (lo + hi + 1) >> 1;
+            if (gtile[mid] <= mt) lo = mid; else hi = mid - 1;
+        }
+        g = lo;
+        row0 = gstart[g] + (mt - gtile[g]) * kPfBM;
+        row1 = min(row0 + kPfBM, gstart[g + 1]);
+        n0 = nt * per_tile;
+    };
+
+    if (warp < kPfProducerWarps) {
+        // ------------------------------------------------------------------------ producers
+        const int t = threadIdx.x;   // 0..255: activation row t / 2 and weight row t / 2, block t % 2 of each stage
+        const int r = t >> 1, hb = t & 1;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
+            int g, row0, row1, n0;
+            tile_of(tile, g, row0, row1, n0);
+            const BlockQ8_1* xrow = nullptr;
+            if (row0 + r < row1) xrow = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row0 + r) : row0 + r) * nb;
+            const uint8_t* wrow = nullptr;
+            {
+                const uint8_t* base = p.blobs + (size_t) g * p.blob_stride + p.w_off;
+                if (MODE == PF_GU) {
+                    const int j = n0 + (r & 63);
+                    if (j < p.N) wrow = base + (r >= 64 ? p.up_off : 0) + (size_t) j * p.w_row;
+                } else {
+                    const int j = n0 + r;
+                    if (j < p.N) wrow = base + (size_t) j * p.w_row;
+                }
+            }
+            for (int ks = 0; ks < nks; ++ks, ++it) {
+                const int s = (int) (it % kPfStages);
+                if (it >= (uint32_t) kPfStages) {
+                    const uint32_t par = ((it / kPfStages) - 1) & 1u;
+                    const uint64_t t0 = globaltimer();
+                    bool ok = true;
+                    while (!mbar_try_wait(&empty[s], par))
+                        if (globaltimer() - t0 > kWaitNs || abort_flag) {
+                            ok = false;
+                            break;
+                        }
+                    if (!ok) {
+                        report_error(p.err, 0x501u);
+                        abort_flag = 1;
+                        break;
+                    }
+                }
+                uint8_t* sa = smem + s * kPfStage;
+                uint8_t* sbh = sa + kPfTileA;
+                uint8_t* sbl = sbh + kPfTileB;
+                const int blk = 2 * ks + hb;
+                if (xrow) stage_q8_codes(xrow + blk, sa, r, hb); else stage_zero(sa, r, hb);
+                if (wrow) {
+                    stage_q4_0(wrow + (size_t) blk * 18, sbh, sbl, r, hb);
+                } else {
+                    stage_zero(sbh, r, hb);
+                    stage_zero(sbl, r, hb);
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
+            }
+        }
+    } else if (warp == kPfMmaWarp) {
+        // ------------------------------------------------------------------------ MMA issue
+        if (lane == 0) {
+            uint32_t it = 0, gb = 0;   // ring stage counter, block counter (both across tiles)
+            for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
+                bool ok = true;
+                for (int kb = 0; kb < nb; ++kb, ++gb) {
+                    const int s = (int) (it % kPfStages);
+                    if ((kb & 1) == 0 && !mbar_wait_bounded(&full[s], (it / kPfStages) & 1u, p.err, 0x503u)) {
+                        ok = false;
+                        break;
+                    }
+                    const int b = (int) (gb % kPfSBuf);
+                    if (gb >= (uint32_t) kPfSBuf &&
+                        !mbar_wait_bounded(&s_empty[b], ((gb / kPfSBuf) - 1) & 1u, p.err, 0x502u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(smem + s * kPfStage) + (uint32_t) (kb & 1) * 64;
+                    const uint32_t bh = a0 + kPfTileA, bl = bh + kPfTileB;
+                    const uint32_t d = tmem + (uint32_t) b * kPfBN;
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        pf_mma(d, pf_sdesc(a0 + kk * 32), pf_sdesc(bh + kk * 32), kk ? 1u : 0u);
+                        pf_mma(d, pf_sdesc(a0 + kk * 32), pf_sdesc(bl + kk * 32), 1u);
+                    }
+                    pf_commit(&s_full[b]);
+                    if (kb & 1) {
+                        pf_commit(&empty[s]);
+                        ++it;
+                    }
+                }
+                if (!ok) {
+                    abort_flag = 1;
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------------------ epilogue (warps 9-12)
+        const int q = warp & 3;   // the TMEM lane quarter this warp may access
+        const uint32_t lane_base = tmem + ((uint32_t) (q * 32) << 16);
+        const uint32_t acc = lane_base + kPfAccCol;
+        uint32_t gb = 0;
+        for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
+            int g, row0, row1, n0;
+            tile_of(tile, g, row0, row1, n0);
+            const int row = row0 + q * 32 + lane;
+            const BlockQ8_1* xrow = nullptr;
+            if (row < row1) xrow = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row) : row) * nb;
+            float dx_next = xrow ? __half2float(__low2half(__ldg(&xrow[0].ds))) : 0.0f;
+            bool ok = true;
+            for (int kb = 0; kb < nb; ++kb, ++gb) {
+                const int b = (int) (gb % kPfSBuf);
+                const float dx = dx_next;
+                if (kb + 1 < nb) dx_next = xrow ? __half2float(__low2half(__ldg(&xrow[kb + 1].ds))) : 0.0f;
+                if (lane == 0) ok = mbar_wait_bounded(&s_full[b], (gb / kPfSBuf) & 1u, p.err, 0x504u);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+                __syncwarp();
+                tc_fence_after();
+                const uint32_t sb = lane_base + (uint32_t) b * kPfBN;
+#pragma unroll 1
+                for (int c = 0; c < kPfBN; c += 32) {
+                    float sv[32], av[32];
+                    tmem_ld32(sb + c, sv);
+                    if (kb > 0) tmem_ld32(acc + c, av);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) av[j] = kb > 0 ? fmaf(sv[j], dx, av[j]) : sv[j] * dx;
+                    tmem_st32(acc + c, av);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[b]);
+            }
+            if (!ok) {
+                abort_flag = 1;
+                break;
+            }
+            // the tile's sums: gate/up -> activation -> q8_1; down -> fp32
+            if (MODE == PF_GU) {
+                float h[64];
+#pragma unroll
+                for (int c = 0; c < 64; c += 32) {
+                    float gv[32], uv[32];
+                    tmem_ld32(acc + c, gv);
+                    tmem_ld32(acc + 64 + c, uv);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        h[c + j] = act_value(p.act, gv[j] * kPfWUnscale, uv[j] * kPfWUnscale, p.limit);
+                }
+                if (row < row1) {
+#pragma unroll
+                    for (int blk = 0; blk < 2; ++blk) {
+                        if (n0 + 32 * blk >= p.N) break;
+                        float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            amax = fmaxf(amax, fabsf(h[32 * blk + j]));
+                            sum += h[32 * blk + j];
+                        }
+                        const float d = q8_finite(fdiv_fm(amax, 127.0f));
+                        uint32_t* o = (uint32_t*) (p.Hq + (size_t) row * (p.N / 32) + (n0 / 32) + blk);
+                        const half2 ds = make_half2(__float2half(d), __float2half(q8_finite(sum)));
+                        o[0] = *(const uint32_t*) &ds;
+#pragma unroll
+                        for (int w = 0; w < 8; ++w) {
+                            uint32_t word = 0;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                int c = 0;
+                                if (amax != 0.0f) {
+                                    const float rq = roundf(fdiv_fm(h[32 * blk + 4 * w + k], d));
+                                    c = (int) (rq > 127.0f ? 127.0f : rq < -127.0f ? -127.0f : rq);
+                                }
+                                word |= (uint32_t) (uint8_t) (int8_t) c << (8 * k);
+                            }
+                            o[1 + w] = word;
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kPfBN; c += 32) {
+                    float v[32];
+                    tmem_ld32(acc + c, v);
+                    tmem_wait_ld();
+                    if (row < row1 && n0 + c < p.N) {
+                        float4* dst = (float4*) (p.D + (size_t) row * p.N + n0 + c);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            dst[j] = make_float4(v[4 * j] * kPfWUnscale, v[4 * j + 1] * kPfWUnscale,
+                                                 v[4 * j + 2] * kPfWUnscale, v[4 * j + 3] * kPfWUnscale);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kPfMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
+// ------------------------------------------------------------------------------------------------ dispatch
+// bounds[e] = number of entries routed to experts < e (bounds[E] = the entries placed); one CTA.
+__global__ void __launch_bounds__(1024) k_dispatch_count(const int32_t* __restrict__ ids, int n_ent, int E,
+                                                         int32_t* __restrict__ bounds, int32_t* __restrict__ rinv) {
+    __shared__ int32_t cnt[1024];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_ent; i += blockDim.x) {
+        const int id = ids[i];
+        if (id >= 0 && id < E) atomicAdd(&cnt[id], 1);
+        rinv[i] = -1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int e = 0; e < E; ++e) {
+            const int c = cnt[e];
+            bounds[e] = s;
+            s += c;
+        }
+        bounds[E] = s;
+    }
+}
+// One CTA per expert: its entries in entry order (a stable sort by expert) -> rows bounds[e]...; row_ent[row] = entry,
+// row_tok[row] = entry / K, rinv[entry] = row.
+__global__ void __launch_bounds__(1024) k_dispatch_scatter(const int32_t* __restrict__ ids, int n_ent, int K,
+                                                           const int32_t* __restrict__ bounds,
+                                                           int32_t* __restrict__ row_ent, int32_t* __restrict__ row_tok,
+                                                           int32_t* __restrict__ rinv) {
+    __shared__ int32_t wsum[32];
+    __shared__ int32_t base_s;
+    const int e = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) base_s = bounds[e];
+    __syncthreads();
+    for (int i0 = 0; i0 < n_ent; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const bool f = i < n_ent && ids[i] == e;
+        const unsigned m = __ballot_sync(0xffffffffu, f);
+        if (lane == 0) wsum[warp] = __popc(m);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < (int) (blockDim.x >> 5); ++w) {
+            before += w < warp ? wsum[w] : 0;
+            total += wsum[w];
+        }
+        if (f) {
+            const int row = base_s + before + __popc(m & ((1u << lane) - 1u));
+            row_ent[row] = i;
+            row_tok[row] = i / K;
+            rinv[i] = row;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) base_s += total;
+        __syncthreads();
+    }
+}
+
+}  // namespace tsb
