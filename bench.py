@@ -145,6 +145,98 @@ def build_stack(cfg, T, device, seed=1):
     return st, layers, x0
 
 
+PREFILL_METRIC = "MoE-layer tokens/s (prefill, Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192)"
+# int8 operations per layer of the C2 configuration: 2 T (K 3 H F + 3 H FS) + router 2 T H E (algorithmic, the
+# reference's MMQ work; the kernels here issue two fp16 tensor-core products per block, hi and lo weight parts)
+def prefill_ops(T, H, F, FS, K, E):
+    return 2.0 * T * (K * 3 * H * F + 3 * H * FS) + 2.0 * T * H * E
+
+
+def bench_prefill(args):
+    """C2: one Gemma-4-26B-A4B-shaped layer (128 Q4_0 experts, top-8, dense Q4_0 shared FFN 2112, GELU-tanh) over
+    T = 8192 prompt tokens: router GEMM, routing, q8_1, dispatch, grouped gate/up + down on tcgen05, shared FFN,
+    combine, replayed as one CUDA graph."""
+    import torch
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+    from tinystrata_b200.layer import PrefillLayer
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    cfg = synth.GEMMA
+    T, H, F, FS, K, E = args.tokens, cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
+    st = synth.device_layers(cfg, 1, seed=2, device=device)
+    escale = torch.ones(E, dtype=torch.float32, device=device)
+    P = PrefillLayer(cfg, st["blobs"][0], st["routers"][0], st["sh_blobs"][0], max_tokens=T, escale=escale)
+    rng = np.random.default_rng(2)
+    x0 = synth.rms_normed(rng, T, H)
+    x0_dev = torch.from_numpy(x0).to(device)
+    x0_host = torch.from_numpy(x0).pin_memory()
+    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    x = torch.empty_like(x0_dev)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        x.copy_(x0_dev)
+        P.forward(x, x0_dev, stream=stream)   # eager pass (allocations, kernel attributes)
+    stream.synchronize()
+    assert TS.device_error() == 0
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        x.copy_(x0_dev)
+        P.forward(x, x0_dev, stream=stream)
+    ge = torch.cuda.CUDAGraph()   # end to end: host input in, result out, each step
+    with torch.cuda.graph(ge, stream=stream):
+        x0_dev.copy_(x0_host, non_blocking=True)
+        x.copy_(x0_dev)
+        P.forward(x, x0_dev, stream=stream)
+        out_host.copy_(x, non_blocking=True)
+
+    def timed(gr, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(n):
+                gr.replay()
+            e1.record(stream)
+        stream.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    timed(g, max(3, args.warmup))
+    with Clocks(local) as clk:
+        ms = timed(g, args.steps)
+    ms_e2e = timed(ge, max(3, args.steps // 2))
+    assert TS.device_error() == 0
+    ops = prefill_ops(T, H, F, FS, K, E)
+    peak = 1647.6
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        peak_kind = "measured bf16 dense (the fp16 tensor-core rate)"
+    except (OSError, KeyError, ValueError):
+        peak_kind = "fallback"
+    achieved = ops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_1 x Q4_0 exact block dots on tcgen05 (fp16 operands: codes, weight hi + lo), fp32 block scaling",
+        "data": "synthetic",
+        "config": {"workload": f"prefill T={T} through one Gemma-4-26B-A4B-shaped MoE layer", "tokens": T, "hidden": H,
+                   "experts": E, "top_k": K, "n_ff": F, "shared_n_ff": FS, "weights": "Q4_0",
+                   "l2": "inputs larger than L2 (428 MB of expert weights)"},
+        "us_per_layer": ms * 1e3,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s (int8-op/s, algorithmic)",
+                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_ops_per_layer": ops},
+        "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
+        "clocks": clk.summary(), "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+    del g, ge
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -155,7 +247,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192)")
     args = ap.parse_args()
+    if args.workload == "prefill":
+        if args.tokens == 1:
+            args.tokens = 8192
+        return bench_prefill(args)
     global N_LAYERS
     N_LAYERS = args.layers
     if args.impl == "reference":

@@ -111,3 +111,24 @@ def test_prefill_rejects_unsupported(cuda):
     xq = torch.zeros((4, cfg["n_embd"] // 32 * 36), dtype=torch.uint8, device="cuda")
     with pytest.raises(T.TsbError, match="status -2"):
         T.moe_prefill_gu(L, blobs, int(L.bytes), None, 1, 4, xq)
+
+
+def test_prefill_layer_gemma_vs_oracle(cuda):
+    """The whole prompt-path layer (router GEMM, routing, q8_1, dispatch, grouped products, shared FFN, combine)."""
+    from tinystrata_b200.layer import PrefillLayer
+    cfg = dict(synth.GEMMA, n_expert=16)
+    H = cfg["n_embd"]
+    layer = synth.make_layer(cfg, 41)
+    rng = np.random.default_rng(41)
+    T_tok = 100
+    x = synth.rms_normed(rng, T_tok, H)
+    P = PrefillLayer(cfg, dev(layer["blobs"]), dev(layer["router"]), dev(layer["sh_blob"]), max_tokens=T_tok,
+                     escale=dev(layer["escale"]))
+    xd = torch.zeros((T_tok, H), device="cuda")
+    P.forward(xd, dev(x))
+    torch.cuda.synchronize()
+    assert T.device_error() == 0
+    ref = O.moe_layer(layer, x)
+    assert np.array_equal(P.ids.cpu().numpy(), ref["ids"])
+    err, cos = tol(xd.cpu().numpy(), ref["out"])
+    assert err <= 1e-2 and cos >= 0.9999, (err, cos)

@@ -597,6 +597,46 @@ int tsb_quantize_q8_1_rows(const float* x, int64_t n_rows, int64_t n_cols, void*
     return cuda_status("quantize_q8_1_rows");
 }
 
+// Many tokens (prefill): 64 tokens x 64 outputs per CTA, each thread 4 x 4 of them, K in smem tiles of 32; every
+// logit is the plain fp32 sum over its inputs in order.
+__global__ void __launch_bounds__(256) k_router_logits_tiled(const float* __restrict__ W, const float* __restrict__ h,
+                                                             float* __restrict__ logits, int n_in, int n_out, int n_tok,
+                                                             int ld) {
+    __shared__ float xs[32][64 + 4], ws[32][64 + 4];   // [k][token], [k][output]
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int o0 = blockIdx.x * 64, t0 = blockIdx.y * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < n_in; k0 += 32) {
+        for (int i = threadIdx.x; i < 64 * 8; i += 256) {   // 64 rows x 8 float4 of K
+            const int row = i >> 3, c4 = i & 7;
+            float4 xv = make_float4(0.f, 0.f, 0.f, 0.f), wv = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + row < n_tok && k0 + 4 * c4 < n_in) xv = __ldg((const float4*) (h + (size_t) (t0 + row) * n_in + k0) + c4);
+            if (o0 + row < n_out && k0 + 4 * c4 < n_in) wv = __ldg((const float4*) (W + (size_t) (o0 + row) * n_in + k0) + c4);
+            xs[4 * c4][row] = xv.x; xs[4 * c4 + 1][row] = xv.y; xs[4 * c4 + 2][row] = xv.z; xs[4 * c4 + 3][row] = xv.w;
+            ws[4 * c4][row] = wv.x; ws[4 * c4 + 1][row] = wv.y; ws[4 * c4 + 2][row] = wv.z; ws[4 * c4 + 3][row] = wv.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float4 a = *(const float4*) &xs[k][ty * 4];
+            const float4 b = *(const float4*) &ws[k][tx * 4];
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int t = t0 + ty * 4 + i, o = o0 + tx * 4 + j;
+            if (t < n_tok && o < n_out) logits[(size_t) t * ld + o] = acc[i][j];
+        }
+}
+
 int tsb_router_logits_f32(const float* W, const float* h, float* logits, int n_in, int n_out, int n_tok, int ld,
                           void* stream) {
     if (!W || !h || !logits || n_in % 4 != 0 || n_tok < 0 || ld < n_out || !aligned(W, 16) || !aligned(h, 16))
@@ -604,6 +644,11 @@ int tsb_router_logits_f32(const float* W, const float* h, float* logits, int n_i
     if (n_tok == 0) return TSB_OK;
     DevInfo* di = dev_info();
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    if (n_tok > 64) {   // prefill: tiled over tokens and outputs
+        k_router_logits_tiled<<<dim3((unsigned) ((n_out + 63) / 64), (unsigned) ((n_tok + 63) / 64)), 256, 0,
+                                cs(stream)>>>(W, h, logits, n_in, n_out, n_tok, ld);
+        return cuda_status("router_logits_f32");
+    }
     const int ctas = std::min((n_out + 7) / 8, di->sms * 4);
     k_router_logits<<<ctas, 256, 0, cs(stream)>>>(W, h, logits, n_in, n_out, n_tok, ld);
     return cuda_status("router_logits_f32");

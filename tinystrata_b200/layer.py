@@ -98,3 +98,57 @@ class MoELayer:
             if shared is not None:
                 x.add_(shared)
         return x
+
+
+class PrefillLayer:
+    """One MoE layer's prompt path for up to max_tokens tokens on the tensor cores (the reference's call stack C, the
+    prompt branch: router, routing, permutation, MMQ gate/up + activation, MMQ down, shared expert, moe_sum;
+    src/gemma4/engine.cpp:2436-2457 with src/prefill/moe_mmq.cu:334-384).  Weights as MoELayer's; Q4_0 experts."""
+
+    def __init__(self, cfg: dict, blobs, router, sh_blob=None, max_tokens: int = 8192, escale=None, bias=None):
+        import torch
+        from . import (Q8_1_BYTES, native_expert_layout)
+        self.cfg = cfg
+        self.H, self.F, self.E, self.K = cfg["n_embd"], cfg["n_ff"], cfg["n_expert"], cfg["n_used"]
+        self.blobs, self.router, self.sh_blob = blobs, router.contiguous(), sh_blob
+        self.L = native_expert_layout(cfg["gu_type"], cfg["d_type"], self.H, self.F)
+        self.stride = int(blobs.stride(0))
+        self.escale, self.bias = escale, bias
+        dev = blobs.device
+        T, K, H = max_tokens, self.K, self.H
+        self.logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
+        self.xq = torch.empty((T, H // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
+        self.hq = torch.empty((T * K, self.F // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
+        self.parts = torch.empty((T * K, H), dtype=torch.float32, device=dev)
+        self.Ls = None
+        if sh_blob is not None and cfg.get("sh_n_ff"):
+            self.Ls = native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, cfg["sh_n_ff"])
+            self.sh_hq = torch.empty((T, cfg["sh_n_ff"] // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
+            self.shared = torch.empty((T, H), dtype=torch.float32, device=dev)
+
+    def forward(self, x, h, stream=None):
+        """x += MoE(h) for T = x.shape[0] tokens (h fp32 [T, H], the layer's normed input)."""
+        from . import (moe_combine, moe_dispatch, moe_prefill_down, moe_prefill_gu, quantize_q8_1_rows, route_rows,
+                       router_logits_f32)
+        cfg = self.cfg
+        T = x.shape[0]
+        K, E = self.K, self.E
+        logits = router_logits_f32(self.router[:E], h, self.logits[:T], stream=stream)
+        if cfg["router_mode"] == "softmax_scaled":
+            ids, w = route_rows(logits, K, 0, cfg.get("in_scale", 1.0), None, self.escale, True, 0.0, stream=stream)
+        else:
+            ids, w = route_rows(logits, K, 1, 1.0, self.bias, None, True, cfg.get("w_scale", 0.0), stream=stream)
+        xq = quantize_q8_1_rows(h, self.xq[:T], stream=stream)
+        bounds, row_ent, row_tok, rinv = moe_dispatch(ids, E, stream=stream)
+        n = T * K
+        hq = moe_prefill_gu(self.L, self.blobs, self.stride, bounds, E, n, xq, row_tok, cfg["act"],
+                            cfg.get("limit", float("inf")), h=self.hq[:n], stream=stream)
+        parts = moe_prefill_down(self.L, self.blobs, self.stride, bounds, E, n, hq, out=self.parts[:n], stream=stream)
+        shared = None
+        if self.Ls is not None:
+            sh = moe_prefill_gu(self.Ls, self.sh_blob, 0, None, 1, T, xq, None, cfg.get("sh_act", cfg["act"]),
+                                cfg.get("limit", float("inf")), h=self.sh_hq[:T], stream=stream)
+            shared = moe_prefill_down(self.Ls, self.sh_blob, 0, None, 1, T, sh, out=self.shared[:T], stream=stream)
+        moe_combine(x, parts, w, K, shared=shared, prow=rinv, stream=stream)
+        self.ids, self.w, self.rinv = ids, w, rinv
+        return x
