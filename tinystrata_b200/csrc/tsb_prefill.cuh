@@ -5,28 +5,26 @@
 // moe_mmq.hpp:58-81; permutation q36_engine.cu:486-510; SwiGLU moe_mmq.cu:123-131): per 32-value block an exact
 // integer dot of the q8_1 activation codes with the weight codes, scaled by both blocks' scales and summed in fp32.
 // The same arithmetic here, on tcgen05:
-//   * per 32-value block the tensor core forms S = sum_k q_x[k] * (d_w * (q_w[k] - 8)) exactly: the activation codes
-//     are exact in fp16 and the weight values d_w (q_w - 8) (15 significant bits) are split into fp16 hi + lo parts
-//     (exact), so two fp16 MMAs per 16 values accumulate integers times exact weights over just 32 terms;
-//   * the epilogue warps then add S * d_x (the activation block's scale) into an fp32 accumulator, block after block,
-//     with round-to-nearest FMAs, as the reference's scale-and-sum does.
+//   * per 32-value block the tensor core forms the integer S = sum_k q_x[k] (q_w[k] - 8) exactly (codes and centred
+//     nibbles are exact in fp16, and every partial sum is an integer far below 2^24);
+//   * the epilogue warps then add S * (d_w d_x) into fp32 accumulators held in registers, block after block, with
+//     round-to-nearest FMAs, as the reference's scale-and-sum does.
 // The hidden vector between the products is re-quantised to q8_1 as the reference's quantiser does, so it is the
-// reference's but for values within fp32 rounding of a code boundary.  Weight values are scaled by 2^10 before the
-// split (exact; undone in the epilogue) so that the lo parts of small weights stay out of fp16's subnormal range
-// (|d_w| <= 8 keeps 8 |d_w| 2^10 below fp16's maximum).
+// reference's but for values within fp32 rounding of a code boundary.
 //
 // Kernel shape (one CTA per SM, persistent over output tiles of 128 rows x 128 columns):
-//   warps 0-7   producers: per ring stage (64 values of K) 128 activation rows (two q8_1 blocks each -> fp16 codes)
-//               and 128 weight rows (two Q4_0 blocks -> fp16 hi and lo), in the tensor core's K-major 128-byte
-//               swizzled layout;
-//   warp 8      tensor-memory allocation and the MMA issue (one thread): per 32-value block 4 x tcgen05.mma M128 N128
-//               K16 into one of three block-sum buffers; tcgen05.commit hands the buffer to the epilogue and, every
-//               second block, frees the ring stage;
-//   warps 9-12  epilogue: per block, tcgen05.ld of the block sums and one FMA with the row's activation scale into
-//               the tensor-memory accumulator (tcgen05.ld / tcgen05.st); at the end of the tile the activation and the
-//               q8_1 quantisation (gate/up) or the fp32 store (down).
-// Gate/up tiles interleave the matrices: B rows 0..63 are gate rows j0..j0+63, rows 64..127 the up rows, so one
-// thread holds the gate and up sums of the same 64 hidden values.
+//   warps 0-1   producers: per ring stage (64 values of K) 128 activation rows (two q8_1 blocks each -> fp16 codes)
+//               and 128 weight rows (two Q4_0 blocks -> fp16 centred nibbles, and their scales), in the tensor core's
+//               K-major 128-byte-swizzled layout; a thread stages two activation rows and two weight rows;
+//   warp 2      tensor-memory allocation and the MMA issue (one thread): per 32-value block 2 x tcgen05.mma M128 N128
+//               K16 into one of three block-sum buffers; tcgen05.commit hands the buffer to the epilogue;
+//   warps 3-10  epilogue: two warps per TMEM lane quarter, a thread owns one output row and 64 columns of the tile;
+//               per block, two tcgen05.ld of its 64 block sums and one FMA each with d_w d_x into 64 register
+//               accumulators; at the end of the tile the activation and the q8_1 quantisation (gate/up) or the fp32
+//               store (down).  A ring stage is free again once the MMAs read it and the epilogue read its scales.
+// Gate/up tiles interleave the matrices in 32-row groups: B rows 0..31 are gate rows j0..j0+31, 32..63 the up rows of
+// the same hidden values, 64..95 gate rows j0+32.., 96..127 their up rows, so a thread's 64 columns are the gate and up
+// sums of one q8_1 block of 32 hidden values.
 #pragma once
 
 #include "tsb_kernels.cuh"
@@ -35,17 +33,16 @@
 
 namespace tsb {
 
-constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 4, kPfSBuf = 3;
-constexpr int kPfProducerWarps = 8, kPfMmaWarp = 8, kPfWarps = 13;
+constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 6, kPfSBuf = 3;
+constexpr int kPfProducerWarps = 2, kPfMmaWarp = 2, kPfEpiWarp0 = 3, kPfEpiWarps = 8, kPfWarps = 11;
 constexpr int kPfThreads = kPfWarps * 32;
 constexpr uint32_t kPfTileA = kPfBM * kPfBK * 2, kPfTileB = kPfBN * kPfBK * 2;   // 16 KB each
-constexpr uint32_t kPfStage = kPfTileA + 2 * kPfTileB;                          // A | B_hi | B_lo
+constexpr uint32_t kPfStageScales = 2 * 2 * kPfBN * 4;   // d_w [2 blocks][128 rows], then d_x [2 blocks][128 rows]
+constexpr uint32_t kPfStage = kPfTileA + kPfTileB + kPfStageScales;             // A | B | scales
 constexpr uint32_t kPfSmem = kPfStages * kPfStage + 1024;   // + slack (swizzled tiles sit on 1 KB)
 constexpr int kPfMaxGroups = 512;
-constexpr uint32_t kPfAccCol = kPfSBuf * kPfBN;             // TMEM columns: 3 block-sum buffers, then the accumulator
 // instruction descriptor: D f32, A f16, B f16, both K-major, N = 128, M = 128
 constexpr uint32_t kPfIdesc = (1u << 4) | ((uint32_t) (kPfBN >> 3) << 17) | ((uint32_t) (kPfBM >> 4) << 24);
-constexpr float kPfWScale = 1024.0f, kPfWUnscale = 1.0f / 1024.0f;
 
 enum : int { PF_GU = 0, PF_DOWN = 1 };
 
@@ -124,14 +121,46 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 }
 
 // ------------------------------------------------------------------------------------------------ operand staging
-// One q8_1 block (fp16 d, fp16 sum, 32 int8 codes) -> its codes as fp16 (exact) into chunks 4h..4h+3 of row r:
-// the byte c + 128 under the exponent of 1024 is the fp16 1024 + c + 128, and an exact subtraction of 1152 leaves c.
-__device__ __forceinline__ void stage_q8_codes(const BlockQ8_1* b, uint8_t* tile, int r, int h) {
-    const uint32_t* w = (const uint32_t*) b->qs;
+// The raw bytes of one ring stage for one producer thread: two activation rows and two weight rows, two blocks each,
+// loaded into registers a stage ahead of their conversion (the conversions never wait on a load).
+struct PfRaw {
+    uint32_t a[2][2][9];   // q8_1 block: word 0 = (fp16 d, fp16 sum), words 1..8 the 32 codes
+    uint32_t w[2][2][5];   // Q4_0 block: word 0 = fp16 d, words 1..4 the 16 bytes of nibbles
+};
+__device__ __forceinline__ void pf_load(PfRaw& R, const BlockQ8_1* const (&xrow)[2], const uint8_t* const (&wrow)[2],
+                                        int ks) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+            const int blk = 2 * ks + hb;
+            if (xrow[i]) {
+                const uint32_t* src = (const uint32_t*) (xrow[i] + blk);
+#pragma unroll
+                for (int k = 0; k < 9; ++k) R.a[i][hb][k] = __ldg(src + k);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 9; ++k) R.a[i][hb][k] = 0u;
+            }
+            if (wrow[i]) {
+                const uint16_t* s16 = (const uint16_t*) (wrow[i] + (size_t) blk * 18);
+                R.w[i][hb][0] = __ldg(s16);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    R.w[i][hb][1 + k] = (uint32_t) __ldg(s16 + 1 + 2 * k) | ((uint32_t) __ldg(s16 + 2 + 2 * k) << 16);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 5; ++k) R.w[i][hb][k] = 0u;
+            }
+        }
+}
+// q8_1 codes -> fp16 (exact) into chunks 4h..4h+3 of row r: the byte c + 128 under the exponent of 1024 is the fp16
+// 1024 + c + 128, and an exact subtraction of 1152 leaves c.
+__device__ __forceinline__ void stage_q8_codes(const uint32_t (&blk)[9], uint8_t* tile, int r, int h) {
     const half2 bias = __float2half2_rn(1152.0f);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {   // 8 codes: words 2c, 2c+1
-        const uint32_t w0 = __ldg(w + 2 * c) ^ 0x80808080u, w1 = __ldg(w + 2 * c + 1) ^ 0x80808080u;
+    for (int c = 0; c < 4; ++c) {   // 8 codes: words 1 + 2c, 2 + 2c
+        const uint32_t w0 = blk[1 + 2 * c] ^ 0x80808080u, w1 = blk[2 + 2 * c] ^ 0x80808080u;
         uint32_t out[4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {   // codes 2p, 2p+1 of the chunk
@@ -142,40 +171,25 @@ __device__ __forceinline__ void stage_q8_codes(const BlockQ8_1* b, uint8_t* tile
         *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(out[0], out[1], out[2], out[3]);
     }
 }
-
-// One Q4_0 block (18 bytes at src: fp16 d, 16 bytes of nibbles; 2-byte aligned) of row r -> chunks 4h..4h+3 of the hi
-// and lo tiles: w = d 2^10 (q - 8) (exact in fp32), hi = fp16(w), lo = fp16(w - hi).  Values 0..15 of a block are the
-// low nibbles of bytes 0..15, values 16..31 the high nibbles.
-__device__ __forceinline__ void stage_q4_0(const uint8_t* src, uint8_t* hi_tile, uint8_t* lo_tile, int r, int h) {
-    const uint16_t* s16 = (const uint16_t*) src;
-    const float d = __half2float(__ushort_as_half(__ldg(s16))) * kPfWScale;
-    uint32_t qs[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) qs[i] = (uint32_t) __ldg(s16 + 1 + 2 * i) | ((uint32_t) __ldg(s16 + 2 + 2 * i) << 16);
+// Q4_0 centred nibbles q - 8 -> fp16 (exact) into chunks 4h..4h+3 of row r.  Values 0..15 of a block are the low
+// nibbles of bytes 0..15, values 16..31 the high nibbles; 0x6400 | q is the fp16 1024 + q, minus 1032 leaves q - 8.
+__device__ __forceinline__ void stage_q4_0(const uint32_t (&blk)[5], uint8_t* tile, int r, int h) {
+    const half2 bias = __float2half2_rn(1032.0f);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {   // chunk c: values 8c..8c+7 (c < 2 low nibbles, c >= 2 high nibbles)
-        const uint32_t q0 = qs[(c & 1) * 2], q1 = qs[(c & 1) * 2 + 1];
+        const uint32_t q0 = blk[1 + (c & 1) * 2], q1 = blk[2 + (c & 1) * 2];
         const int sh = (c >> 1) * 4;
-        uint32_t oh[4], ol[4];
+        uint32_t out[4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const uint32_t src8 = p < 2 ? q0 : q1;
-            const int byte = (p & 1) * 2;
-            const float v0 = d * (float) ((int) ((src8 >> (8 * byte + sh)) & 0xF) - 8);
-            const float v1 = d * (float) ((int) ((src8 >> (8 * (byte + 1) + sh)) & 0xF) - 8);
-            const half2 vh = __floats2half2_rn(v0, v1);
-            const float2 vhf = __half22float2(vh);
-            const half2 vl = __floats2half2_rn(v0 - vhf.x, v1 - vhf.y);
-            oh[p] = *(const uint32_t*) &vh;
-            ol[p] = *(const uint32_t*) &vl;
+        for (int p = 0; p < 4; ++p) {   // values 2p, 2p+1: bytes 2p, 2p+1 of the 8 source bytes
+            const uint32_t x = (p < 2 ? q0 : q1) >> ((p & 1) * 16);
+            const uint32_t lo = (x >> sh) & 0xFu, hi = (x >> (8 + sh)) & 0xFu;
+            const uint32_t bits = 0x64006400u | lo | (hi << 16);
+            const half2 v = __hsub2(*(const half2*) &bits, bias);
+            out[p] = *(const uint32_t*) &v;
         }
-        *(uint4*) (hi_tile + sw128(r, 4 * h + c)) = make_uint4(oh[0], oh[1], oh[2], oh[3]);
-        *(uint4*) (lo_tile + sw128(r, 4 * h + c)) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+        *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(out[0], out[1], out[2], out[3]);
     }
-}
-__device__ __forceinline__ void stage_zero(uint8_t* tile, int r, int h) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(0, 0, 0, 0);
 }
 
 // ------------------------------------------------------------------------------------------------ the kernel
@@ -193,11 +207,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPfStages; ++s) {
             mbar_init(&full[s], kPfProducerWarps);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], 1 + kPfEpiWarps);   // the MMAs' commit and every epilogue warp (scales read)
         }
         for (int b = 0; b < kPfSBuf; ++b) {
             mbar_init(&s_full[b], 1);
-            mbar_init(&s_empty[b], 4);
+            mbar_init(&s_empty[b], kPfEpiWarps);
         }
         abort_flag = 0;
         fence_mbar_init();
@@ -243,26 +257,34 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
 
     if (warp < kPfProducerWarps) {
         // ------------------------------------------------------------------------ producers
-        const int t = threadIdx.x;   // 0..255: activation row t / 2 and weight row t / 2, block t % 2 of each stage
-        const int r = t >> 1, hb = t & 1;
+        // thread t: rows 2t and 2t + 1 of both operands; a stage's raw blocks are loaded while the previous one is
+        // converted
         uint32_t it = 0;
+        PfRaw R;
         for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
             int g, row0, row1, n0;
             tile_of(tile, g, row0, row1, n0);
-            const BlockQ8_1* xrow = nullptr;
-            if (row0 + r < row1) xrow = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row0 + r) : row0 + r) * nb;
-            const uint8_t* wrow = nullptr;
-            {
-                const uint8_t* base = p.blobs + (size_t) g * p.blob_stride + p.w_off;
-                if (MODE == PF_GU) {
-                    const int j = n0 + (r & 63);
-                    if (j < p.N) wrow = base + (r >= 64 ? p.up_off : 0) + (size_t) j * p.w_row;
+            const BlockQ8_1* xrow[2];
+            const uint8_t* wrow[2];
+            const uint8_t* base = p.blobs + (size_t) g * p.blob_stride + p.w_off;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r = 2 * threadIdx.x + i;
+                xrow[i] = nullptr;
+                if (row0 + r < row1) xrow[i] = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row0 + r) : row0 + r) * nb;
+                wrow[i] = nullptr;
+                if (MODE == PF_GU) {   // 32-row groups: gate, up, gate, up
+                    const int j = n0 + (r >> 6) * 32 + (r & 31);
+                    if (j < p.N) wrow[i] = base + ((r & 32) ? p.up_off : 0) + (size_t) j * p.w_row;
                 } else {
                     const int j = n0 + r;
-                    if (j < p.N) wrow = base + (size_t) j * p.w_row;
+                    if (j < p.N) wrow[i] = base + (size_t) j * p.w_row;
                 }
             }
+            pf_load(R, xrow, wrow, 0);
             for (int ks = 0; ks < nks; ++ks, ++it) {
+                const PfRaw cur = R;
+                if (ks + 1 < nks) pf_load(R, xrow, wrow, ks + 1);
                 const int s = (int) (it % kPfStages);
                 if (it >= (uint32_t) kPfStages) {
                     const uint32_t par = ((it / kPfStages) - 1) & 1u;
@@ -280,15 +302,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                     }
                 }
                 uint8_t* sa = smem + s * kPfStage;
-                uint8_t* sbh = sa + kPfTileA;
-                uint8_t* sbl = sbh + kPfTileB;
-                const int blk = 2 * ks + hb;
-                if (xrow) stage_q8_codes(xrow + blk, sa, r, hb); else stage_zero(sa, r, hb);
-                if (wrow) {
-                    stage_q4_0(wrow + (size_t) blk * 18, sbh, sbl, r, hb);
-                } else {
-                    stage_zero(sbh, r, hb);
-                    stage_zero(sbl, r, hb);
+                uint8_t* sb = sa + kPfTileA;
+                float* sdw = (float*) (sb + kPfTileB);   // [2 blocks][128 rows]
+                float* sdx = sdw + 2 * kPfBN;             // [2 blocks][128 rows]
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int r = 2 * threadIdx.x + i;
+#pragma unroll
+                    for (int hb = 0; hb < 2; ++hb) {
+                        stage_q8_codes(cur.a[i][hb], sa, r, hb);
+                        sdx[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (cur.a[i][hb][0] & 0xFFFFu)));
+                        stage_q4_0(cur.w[i][hb], sb, r, hb);
+                        sdw[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (cur.w[i][hb][0] & 0xFFFFu)));
+                    }
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -315,13 +341,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                     }
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(smem + s * kPfStage) + (uint32_t) (kb & 1) * 64;
-                    const uint32_t bh = a0 + kPfTileA, bl = bh + kPfTileB;
+                    const uint32_t b0 = a0 + kPfTileA;
                     const uint32_t d = tmem + (uint32_t) b * kPfBN;
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk) {
-                        pf_mma(d, pf_sdesc(a0 + kk * 32), pf_sdesc(bh + kk * 32), kk ? 1u : 0u);
-                        pf_mma(d, pf_sdesc(a0 + kk * 32), pf_sdesc(bl + kk * 32), 1u);
-                    }
+                    for (int kk = 0; kk < 2; ++kk) pf_mma(d, pf_sdesc(a0 + kk * 32), pf_sdesc(b0 + kk * 32), kk ? 1u : 0u);
                     pf_commit(&s_full[b]);
                     if (kb & 1) {
                         pf_commit(&empty[s]);
@@ -336,43 +359,60 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
         }
         __syncwarp();
     } else {
-        // ------------------------------------------------------------------------ epilogue (warps 9-12)
-        const int q = warp & 3;   // the TMEM lane quarter this warp may access
-        const uint32_t lane_base = tmem + ((uint32_t) (q * 32) << 16);
-        const uint32_t acc = lane_base + kPfAccCol;
+        // ------------------------------------------------------------------------ epilogue (warps 3-10)
+        const int q = warp & 3;                            // the TMEM lane quarter this warp may access
+        const int half = (warp - kPfEpiWarp0) >> 2;        // columns 64 half ..
+        const uint32_t lane_base = tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (64 * half);
         uint32_t gb = 0;
         for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
             int g, row0, row1, n0;
             tile_of(tile, g, row0, row1, n0);
             const int row = row0 + q * 32 + lane;
-            const BlockQ8_1* xrow = nullptr;
-            if (row < row1) xrow = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row) : row) * nb;
-            float dx_next = xrow ? __half2float(__low2half(__ldg(&xrow[0].ds))) : 0.0f;
+            float acc[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
             bool ok = true;
             for (int kb = 0; kb < nb; ++kb, ++gb) {
                 const int b = (int) (gb % kPfSBuf);
-                const float dx = dx_next;
-                if (kb + 1 < nb) dx_next = xrow ? __half2float(__low2half(__ldg(&xrow[kb + 1].ds))) : 0.0f;
-                if (lane == 0) ok = mbar_wait_bounded(&s_full[b], (gb / kPfSBuf) & 1u, p.err, 0x504u);
+                const uint32_t it = gb >> 1;   // the ring stage of this block (two blocks a stage)
+                const int s = (int) (it % kPfStages);
+                if (lane == 0) {
+                    ok = mbar_wait_bounded(&s_full[b], (gb / kPfSBuf) & 1u, p.err, 0x504u);
+                    // the stage's scales: its fill is complete (and cannot be refilled before this warp releases it)
+                    if (ok) ok = mbar_wait_bounded(&full[s], (it / kPfStages) & 1u, p.err, 0x505u);
+                }
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
                 __syncwarp();
                 tc_fence_after();
                 const uint32_t sb = lane_base + (uint32_t) b * kPfBN;
-#pragma unroll 1
-                for (int c = 0; c < kPfBN; c += 32) {
-                    float sv[32], av[32];
-                    tmem_ld32(sb + c, sv);
-                    if (kb > 0) tmem_ld32(acc + c, av);
+                const float* scales = (const float*) (smem + s * kPfStage + kPfTileA + kPfTileB);
+                const float4* dw4 = (const float4*) scales + (kb & 1) * (kPfBN / 4) + 16 * half;
+                const float dx = scales[2 * kPfBN + (kb & 1) * kPfBN + q * 32 + lane];
+                {
+                    float s0[32], s1[32];
+                    tmem_ld32(sb, s0);
+                    tmem_ld32(sb + 32, s1);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) av[j] = kb > 0 ? fmaf(sv[j], dx, av[j]) : sv[j] * dx;
-                    tmem_st32(acc + c, av);
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 w0 = dw4[j4], w1 = dw4[8 + j4];
+                        acc[4 * j4 + 0] = fmaf(w0.x * dx, s0[4 * j4 + 0], acc[4 * j4 + 0]);
+                        acc[4 * j4 + 1] = fmaf(w0.y * dx, s0[4 * j4 + 1], acc[4 * j4 + 1]);
+                        acc[4 * j4 + 2] = fmaf(w0.z * dx, s0[4 * j4 + 2], acc[4 * j4 + 2]);
+                        acc[4 * j4 + 3] = fmaf(w0.w * dx, s0[4 * j4 + 3], acc[4 * j4 + 3]);
+                        acc[32 + 4 * j4 + 0] = fmaf(w1.x * dx, s1[4 * j4 + 0], acc[32 + 4 * j4 + 0]);
+                        acc[32 + 4 * j4 + 1] = fmaf(w1.y * dx, s1[4 * j4 + 1], acc[32 + 4 * j4 + 1]);
+                        acc[32 + 4 * j4 + 2] = fmaf(w1.z * dx, s1[4 * j4 + 2], acc[32 + 4 * j4 + 2]);
+                        acc[32 + 4 * j4 + 3] = fmaf(w1.w * dx, s1[4 * j4 + 3], acc[32 + 4 * j4 + 3]);
+                    }
                 }
-                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s_empty[b]);
+                if (lane == 0) {
+                    mbar_arrive(&s_empty[b]);
+                    if (kb & 1) mbar_arrive(&empty[s]);   // both blocks' scales of the stage read
+                }
             }
             if (!ok) {
                 abort_flag = 1;
@@ -380,27 +420,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
             }
             // the tile's sums: gate/up -> activation -> q8_1; down -> fp32
             if (MODE == PF_GU) {
-                float h[64];
+                // this thread's q8_1 block of hidden values: gate sums acc[j], up sums acc[32 + j]
+                {
+                    const int blk = half;
+                    float h[32], amax = 0.0f, sum = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 64; c += 32) {
-                    float gv[32], uv[32];
-                    tmem_ld32(acc + c, gv);
-                    tmem_ld32(acc + 64 + c, uv);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        h[c + j] = act_value(p.act, gv[j] * kPfWUnscale, uv[j] * kPfWUnscale, p.limit);
-                }
-                if (row < row1) {
-#pragma unroll
-                    for (int blk = 0; blk < 2; ++blk) {
-                        if (n0 + 32 * blk >= p.N) break;
-                        float amax = 0.0f, sum = 0.0f;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            amax = fmaxf(amax, fabsf(h[32 * blk + j]));
-                            sum += h[32 * blk + j];
-                        }
+                    for (int j = 0; j < 32; ++j) {
+                        h[j] = act_value(p.act, acc[j], acc[32 + j], p.limit);
+                        amax = fmaxf(amax, fabsf(h[j]));
+                        sum += h[j];
+                    }
+                    if (row < row1 && n0 + 32 * blk < p.N) {
                         const float d = q8_finite(fdiv_fm(amax, 127.0f));
                         uint32_t* o = (uint32_t*) (p.Hq + (size_t) row * (p.N / 32) + (n0 / 32) + blk);
                         const half2 ds = make_half2(__float2half(d), __float2half(q8_finite(sum)));
@@ -412,7 +442,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                             for (int k = 0; k < 4; ++k) {
                                 int c = 0;
                                 if (amax != 0.0f) {
-                                    const float rq = roundf(fdiv_fm(h[32 * blk + 4 * w + k], d));
+                                    const float rq = roundf(fdiv_fm(h[4 * w + k], d));
                                     c = (int) (rq > 127.0f ? 127.0f : rq < -127.0f ? -127.0f : rq);
                                 }
                                 word |= (uint32_t) (uint8_t) (int8_t) c << (8 * k);
@@ -422,17 +452,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                     }
                 }
             } else {
-#pragma unroll 1
-                for (int c = 0; c < kPfBN; c += 32) {
-                    float v[32];
-                    tmem_ld32(acc + c, v);
-                    tmem_wait_ld();
-                    if (row < row1 && n0 + c < p.N) {
-                        float4* dst = (float4*) (p.D + (size_t) row * p.N + n0 + c);
+#pragma unroll
+                for (int c = 0; c < 64; c += 32) {
+                    const int col = n0 + 64 * half + c;
+                    if (row < row1 && col < p.N) {
+                        float4* dst = (float4*) (p.D + (size_t) row * p.N + col);
 #pragma unroll
                         for (int j = 0; j < 8; ++j)
-                            dst[j] = make_float4(v[4 * j] * kPfWUnscale, v[4 * j + 1] * kPfWUnscale,
-                                                 v[4 * j + 2] * kPfWUnscale, v[4 * j + 3] * kPfWUnscale);
+                            dst[j] = make_float4(acc[c + 4 * j], acc[c + 4 * j + 1], acc[c + 4 * j + 2], acc[c + 4 * j + 3]);
                     }
                 }
             }
