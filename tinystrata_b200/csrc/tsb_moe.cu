@@ -794,19 +794,34 @@ int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t
     return cuda_status("moe_dispatch");
 }
 
+}  // extern "C"
+template <int MODE, bool A16, bool W16>
+static int pf_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
+    auto kern = k_pf_gemm<MODE, A16, W16>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPfSmem) != cudaSuccess)
+            return cuda_status("prefill: shared memory");
+        attr = true;
+    }
+    kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
+    return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
+}
+extern "C" {
+// 16-byte windows where the rows allow them: activation rows of K / 32 q8_1 blocks (36 bytes), weight rows.
 static int pf_launch(int mode, PfParams& pp, cudaStream_t s) {
     DevInfo* di = dev_info();
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
     pp.err = di->err;
-    auto kern = mode == PF_GU ? k_pf_gemm<PF_GU> : k_pf_gemm<PF_DOWN>;
-    static bool attr[2] = {false, false};
-    if (!attr[mode]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPfSmem) != cudaSuccess)
-            return cuda_status("prefill: shared memory");
-        attr[mode] = true;
+    const bool a16 = ((pp.K / 32) * 36) % 16 == 0 && (uintptr_t) pp.X % 16 == 0;
+    const bool w16 = pp.w_row % 16 == 0 && (uintptr_t) pp.blobs % 16 == 0 && pp.blob_stride % 16 == 0 &&
+                     pp.w_off % 16 == 0 && pp.up_off % 16 == 0;
+    if (mode == PF_GU) {
+        if (a16) return w16 ? pf_launch_t<PF_GU, true, true>(pp, s, di) : pf_launch_t<PF_GU, true, false>(pp, s, di);
+        return w16 ? pf_launch_t<PF_GU, false, true>(pp, s, di) : pf_launch_t<PF_GU, false, false>(pp, s, di);
     }
-    kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
-    return cuda_status(mode == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
+    if (a16) return w16 ? pf_launch_t<PF_DOWN, true, true>(pp, s, di) : pf_launch_t<PF_DOWN, true, false>(pp, s, di);
+    return w16 ? pf_launch_t<PF_DOWN, false, true>(pp, s, di) : pf_launch_t<PF_DOWN, false, false>(pp, s, di);
 }
 
 static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, int n_groups, int n_rows,
@@ -817,7 +832,7 @@ static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob
     if (t != T_Q4_0) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0 only)", t);
     if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 128)
         return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd and n_ff multiples of 64, at least 128");
-    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || L->gu_row % 2 || L->d_row % 2)
+    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || L->gu_row % 4 || L->d_row % 4)
         return fail(TSB_ERR_ALIGN, "moe_prefill: blob alignment");
     return TSB_OK;
 }

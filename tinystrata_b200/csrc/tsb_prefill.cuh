@@ -13,12 +13,13 @@
 // reference's but for values within fp32 rounding of a code boundary.
 //
 // Kernel shape (one CTA per SM, persistent over output tiles of 128 rows x 128 columns):
-//   warps 0-1   producers: per ring stage (64 values of K) 128 activation rows (two q8_1 blocks each -> fp16 codes)
+//   warps 0-3   producers: per ring stage (64 values of K) 128 activation rows (two q8_1 blocks each -> fp16 codes)
 //               and 128 weight rows (two Q4_0 blocks -> fp16 centred nibbles, and their scales), in the tensor core's
-//               K-major 128-byte-swizzled layout; a thread stages two activation rows and two weight rows;
-//   warp 2      tensor-memory allocation and the MMA issue (one thread): per 32-value block 2 x tcgen05.mma M128 N128
+//               K-major 128-byte-swizzled layout; a thread stages one activation row and one weight row, loading the
+//               16-byte windows that cover the stage's bytes one stage ahead;
+//   warp 4      tensor-memory allocation and the MMA issue (one thread): per 32-value block 2 x tcgen05.mma M128 N128
 //               K16 into one of three block-sum buffers; tcgen05.commit hands the buffer to the epilogue;
-//   warps 3-10  epilogue: two warps per TMEM lane quarter, a thread owns one output row and 64 columns of the tile;
+//   warps 5-12  epilogue: two warps per TMEM lane quarter, a thread owns one output row and 64 columns of the tile;
 //               per block, two tcgen05.ld of its 64 block sums and one FMA each with d_w d_x into 64 register
 //               accumulators; at the end of the tile the activation and the q8_1 quantisation (gate/up) or the fp32
 //               store (down).  A ring stage is free again once the MMAs read it and the epilogue read its scales.
@@ -34,7 +35,7 @@
 namespace tsb {
 
 constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 6, kPfSBuf = 3;
-constexpr int kPfProducerWarps = 2, kPfMmaWarp = 2, kPfEpiWarp0 = 3, kPfEpiWarps = 8, kPfWarps = 11;
+constexpr int kPfProducerWarps = 4, kPfMmaWarp = 4, kPfEpiWarp0 = 5, kPfEpiWarps = 8, kPfWarps = 13;
 constexpr int kPfThreads = kPfWarps * 32;
 constexpr uint32_t kPfTileA = kPfBM * kPfBK * 2, kPfTileB = kPfBN * kPfBK * 2;   // 16 KB each
 constexpr uint32_t kPfStageScales = 2 * 2 * kPfBN * 4;   // d_w [2 blocks][128 rows], then d_x [2 blocks][128 rows]
@@ -121,38 +122,75 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
 }
 
 // ------------------------------------------------------------------------------------------------ operand staging
-// The raw bytes of one ring stage for one producer thread: two activation rows and two weight rows, two blocks each,
-// loaded into registers a stage ahead of their conversion (the conversions never wait on a load).
+// The raw bytes of one ring stage for one producer thread (one activation row, one weight row), loaded a stage ahead
+// of their conversion.  With 16-byte-aligned rows (A16 / W16) the loads are the 16-byte windows covering the stage:
+// the two q8_1 blocks (72 bytes at 72 ks, five windows from byte 72 ks rounded down to 16) and the two Q4_0 blocks
+// (36 bytes at 36 ks, three windows); otherwise the bytes themselves in 8- and 4-byte words.
 struct PfRaw {
-    uint32_t a[2][2][9];   // q8_1 block: word 0 = (fp16 d, fp16 sum), words 1..8 the 32 codes
-    uint32_t w[2][2][5];   // Q4_0 block: word 0 = fp16 d, words 1..4 the 16 bytes of nibbles
+    uint32_t a[20];
+    uint32_t w[12];
 };
-__device__ __forceinline__ void pf_load(PfRaw& R, const BlockQ8_1* const (&xrow)[2], const uint8_t* const (&wrow)[2],
-                                        int ks) {
+template <bool A16, bool W16>
+__device__ __forceinline__ void pf_load(PfRaw& R, const BlockQ8_1* xrow, const uint8_t* wrow, int ks) {
+    if (xrow) {
+        const uint8_t* src = (const uint8_t*) xrow + 72 * ks;
+        if (A16) {
+            const uint4* v = (const uint4*) ((uintptr_t) src & ~(uintptr_t) 15);
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-            const int blk = 2 * ks + hb;
-            if (xrow[i]) {
-                const uint32_t* src = (const uint32_t*) (xrow[i] + blk);
-#pragma unroll
-                for (int k = 0; k < 9; ++k) R.a[i][hb][k] = __ldg(src + k);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 9; ++k) R.a[i][hb][k] = 0u;
+            for (int k = 0; k < 5; ++k) {
+                const uint4 t = __ldg(v + k);
+                R.a[4 * k] = t.x; R.a[4 * k + 1] = t.y; R.a[4 * k + 2] = t.z; R.a[4 * k + 3] = t.w;
             }
-            if (wrow[i]) {
-                const uint16_t* s16 = (const uint16_t*) (wrow[i] + (size_t) blk * 18);
-                R.w[i][hb][0] = __ldg(s16);
+        } else {
+            const uint2* v = (const uint2*) src;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    R.w[i][hb][1 + k] = (uint32_t) __ldg(s16 + 1 + 2 * k) | ((uint32_t) __ldg(s16 + 2 + 2 * k) << 16);
-            } else {
-#pragma unroll
-                for (int k = 0; k < 5; ++k) R.w[i][hb][k] = 0u;
+            for (int k = 0; k < 9; ++k) {
+                const uint2 t = __ldg(v + k);
+                R.a[2 * k] = t.x; R.a[2 * k + 1] = t.y;
             }
         }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 20; ++k) R.a[k] = 0u;
+    }
+    if (wrow) {
+        const uint8_t* src = wrow + 36 * ks;
+        if (W16) {
+            const uint4* v = (const uint4*) ((uintptr_t) src & ~(uintptr_t) 15);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                const uint4 t = __ldg(v + k);
+                R.w[4 * k] = t.x; R.w[4 * k + 1] = t.y; R.w[4 * k + 2] = t.z; R.w[4 * k + 3] = t.w;
+            }
+        } else {
+            const uint32_t* v = (const uint32_t*) src;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) R.w[k] = __ldg(v + k);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 12; ++k) R.w[k] = 0u;
+    }
+}
+// The q8_1 block hb of the stage as 9 words (scale word, 8 code words): word offset oa / 4 + 9 hb in the window.
+template <int OA>
+__device__ __forceinline__ void pf_a_block(const PfRaw& R, int hb, uint32_t (&b)[9]) {
+#pragma unroll
+    for (int k = 0; k < 9; ++k) b[k] = R.a[OA / 4 + 9 * hb + k];
+}
+// The Q4_0 block hb of the stage as (d word, 4 nibble words): block 0 at byte OB of the window (d, then 16 bytes at
+// OB + 2: two-byte shifted words), block 1 at OB + 18 (d in the high half of word (OB + 16) / 4, nibbles aligned).
+template <int OB>
+__device__ __forceinline__ void pf_w_block(const PfRaw& R, int hb, uint32_t (&b)[5]) {
+    if (hb == 0) {
+        b[0] = R.w[OB / 4] & 0xFFFFu;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) b[1 + k] = __byte_perm(R.w[OB / 4 + k], R.w[OB / 4 + k + 1], 0x5432);
+    } else {
+        b[0] = R.w[(OB + 16) / 4] >> 16;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) b[1 + k] = R.w[(OB + 20) / 4 + k];
+    }
 }
 // q8_1 codes -> fp16 (exact) into chunks 4h..4h+3 of row r: the byte c + 128 under the exponent of 1024 is the fp16
 // 1024 + c + 128, and an exact subtraction of 1152 leaves c.
@@ -193,7 +231,7 @@ __device__ __forceinline__ void stage_q4_0(const uint32_t (&blk)[5], uint8_t* ti
 }
 
 // ------------------------------------------------------------------------------------------------ the kernel
-template <int MODE>
+template <int MODE, bool A16, bool W16>
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
     extern __shared__ __align__(1024) uint8_t pf_raw[];
     uint8_t* smem = (uint8_t*) (((uintptr_t) pf_raw + 1023) & ~(uintptr_t) 1023);
@@ -257,34 +295,31 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
 
     if (warp < kPfProducerWarps) {
         // ------------------------------------------------------------------------ producers
-        // thread t: rows 2t and 2t + 1 of both operands; a stage's raw blocks are loaded while the previous one is
-        // converted
+        // thread r: activation row r and weight row r of every stage; a stage's raw bytes are loaded while the
+        // previous stage is converted
+        const int r = threadIdx.x;
         uint32_t it = 0;
         PfRaw R;
         for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
             int g, row0, row1, n0;
             tile_of(tile, g, row0, row1, n0);
-            const BlockQ8_1* xrow[2];
-            const uint8_t* wrow[2];
-            const uint8_t* base = p.blobs + (size_t) g * p.blob_stride + p.w_off;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int r = 2 * threadIdx.x + i;
-                xrow[i] = nullptr;
-                if (row0 + r < row1) xrow[i] = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row0 + r) : row0 + r) * nb;
-                wrow[i] = nullptr;
+            const BlockQ8_1* xrow = nullptr;
+            if (row0 + r < row1) xrow = p.X + (size_t) (p.row_tok ? __ldg(p.row_tok + row0 + r) : row0 + r) * nb;
+            const uint8_t* wrow = nullptr;
+            {
+                const uint8_t* base = p.blobs + (size_t) g * p.blob_stride + p.w_off;
                 if (MODE == PF_GU) {   // 32-row groups: gate, up, gate, up
                     const int j = n0 + (r >> 6) * 32 + (r & 31);
-                    if (j < p.N) wrow[i] = base + ((r & 32) ? p.up_off : 0) + (size_t) j * p.w_row;
+                    if (j < p.N) wrow = base + ((r & 32) ? p.up_off : 0) + (size_t) j * p.w_row;
                 } else {
                     const int j = n0 + r;
-                    if (j < p.N) wrow[i] = base + (size_t) j * p.w_row;
+                    if (j < p.N) wrow = base + (size_t) j * p.w_row;
                 }
             }
-            pf_load(R, xrow, wrow, 0);
+            pf_load<A16, W16>(R, xrow, wrow, 0);
             for (int ks = 0; ks < nks; ++ks, ++it) {
                 const PfRaw cur = R;
-                if (ks + 1 < nks) pf_load(R, xrow, wrow, ks + 1);
+                if (ks + 1 < nks) pf_load<A16, W16>(R, xrow, wrow, ks + 1);
                 const int s = (int) (it % kPfStages);
                 if (it >= (uint32_t) kPfStages) {
                     const uint32_t par = ((it / kPfStages) - 1) & 1u;
@@ -306,15 +341,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                 float* sdw = (float*) (sb + kPfTileB);   // [2 blocks][128 rows]
                 float* sdx = sdw + 2 * kPfBN;             // [2 blocks][128 rows]
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int r = 2 * threadIdx.x + i;
-#pragma unroll
-                    for (int hb = 0; hb < 2; ++hb) {
-                        stage_q8_codes(cur.a[i][hb], sa, r, hb);
-                        sdx[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (cur.a[i][hb][0] & 0xFFFFu)));
-                        stage_q4_0(cur.w[i][hb], sb, r, hb);
-                        sdw[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (cur.w[i][hb][0] & 0xFFFFu)));
+                for (int hb = 0; hb < 2; ++hb) {
+                    uint32_t ab[9], wb[5];
+                    if (!A16 || (ks & 1) == 0) pf_a_block<0>(cur, hb, ab); else pf_a_block<8>(cur, hb, ab);
+                    if (!W16) {
+                        pf_w_block<0>(cur, hb, wb);
+                    } else {
+                        switch (ks & 3) {
+                            case 0: pf_w_block<0>(cur, hb, wb); break;
+                            case 1: pf_w_block<4>(cur, hb, wb); break;
+                            case 2: pf_w_block<8>(cur, hb, wb); break;
+                            default: pf_w_block<12>(cur, hb, wb); break;
+                        }
                     }
+                    if (xrow) {
+                        stage_q8_codes(ab, sa, r, hb);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) *(uint4*) (sa + sw128(r, 4 * hb + c)) = make_uint4(0, 0, 0, 0);
+                    }
+                    sdx[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (ab[0] & 0xFFFFu)));
+                    stage_q4_0(wb, sb, r, hb);
+                    sdw[hb * kPfBN + r] = __half2float(__ushort_as_half((unsigned short) (wb[0] & 0xFFFFu)));
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -389,22 +437,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                 const float* scales = (const float*) (smem + s * kPfStage + kPfTileA + kPfTileB);
                 const float4* dw4 = (const float4*) scales + (kb & 1) * (kPfBN / 4) + 16 * half;
                 const float dx = scales[2 * kPfBN + (kb & 1) * kPfBN + q * 32 + lane];
-                {
-                    float s0[32], s1[32];
-                    tmem_ld32(sb, s0);
-                    tmem_ld32(sb + 32, s1);
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {   // 32 columns at a time
+                    float sv[32];
+                    tmem_ld32(sb + 32 * hh, sv);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
-                        const float4 w0 = dw4[j4], w1 = dw4[8 + j4];
-                        acc[4 * j4 + 0] = fmaf(w0.x * dx, s0[4 * j4 + 0], acc[4 * j4 + 0]);
-                        acc[4 * j4 + 1] = fmaf(w0.y * dx, s0[4 * j4 + 1], acc[4 * j4 + 1]);
-                        acc[4 * j4 + 2] = fmaf(w0.z * dx, s0[4 * j4 + 2], acc[4 * j4 + 2]);
-                        acc[4 * j4 + 3] = fmaf(w0.w * dx, s0[4 * j4 + 3], acc[4 * j4 + 3]);
-                        acc[32 + 4 * j4 + 0] = fmaf(w1.x * dx, s1[4 * j4 + 0], acc[32 + 4 * j4 + 0]);
-                        acc[32 + 4 * j4 + 1] = fmaf(w1.y * dx, s1[4 * j4 + 1], acc[32 + 4 * j4 + 1]);
-                        acc[32 + 4 * j4 + 2] = fmaf(w1.z * dx, s1[4 * j4 + 2], acc[32 + 4 * j4 + 2]);
-                        acc[32 + 4 * j4 + 3] = fmaf(w1.w * dx, s1[4 * j4 + 3], acc[32 + 4 * j4 + 3]);
+                        const float4 w0 = dw4[8 * hh + j4];
+                        acc[32 * hh + 4 * j4 + 0] = fmaf(w0.x * dx, sv[4 * j4 + 0], acc[32 * hh + 4 * j4 + 0]);
+                        acc[32 * hh + 4 * j4 + 1] = fmaf(w0.y * dx, sv[4 * j4 + 1], acc[32 * hh + 4 * j4 + 1]);
+                        acc[32 * hh + 4 * j4 + 2] = fmaf(w0.z * dx, sv[4 * j4 + 2], acc[32 * hh + 4 * j4 + 2]);
+                        acc[32 * hh + 4 * j4 + 3] = fmaf(w0.w * dx, sv[4 * j4 + 3], acc[32 * hh + 4 * j4 + 3]);
                     }
                 }
                 tc_fence_before();
