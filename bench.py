@@ -237,6 +237,88 @@ def bench_prefill(args):
     return 0
 
 
+EP_METRIC = "EP prefill MoE-layer tokens/s (Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192 per GPU, experts sharded)"
+
+
+def bench_ep(args):
+    """Expert-parallel prefill: the C2 layer's 128 experts sharded 128/N per GPU, T tokens per GPU (weak scaling);
+    per step every rank routes its tokens, the dispatch / return all-to-alls run over NCCL, the local experts on the
+    tensor cores, the dense shared FFN on the rank's own tokens.  Eager (host-synchronising counts), timed with CUDA
+    events between barriers, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+    from tinystrata_b200.ep import ep_forward, gpu_expert_fn
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    else:
+        import tempfile
+        dist.init_process_group("nccl", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1,
+                                device_id=device)
+    cfg = synth.GEMMA
+    T, H, F, FS, K, E = args.tokens, cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
+    per = E // ws
+    st = synth.device_layers(cfg, 1, seed=2, device=device)   # every rank draws the same layer, keeps its slice
+    blobs = st["blobs"][0][rank * per:(rank + 1) * per].contiguous()
+    router, sh = st["routers"][0], st["sh_blobs"][0]
+    del st
+    L = TS.native_expert_layout(cfg["gu_type"], cfg["d_type"], H, F)
+    Ls = TS.native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, FS)
+    escale = torch.ones(E, dtype=torch.float32, device=device)
+    x0 = torch.from_numpy(synth.rms_normed(np.random.default_rng(2 + rank), T, H)).to(device)
+    fn = gpu_expert_fn(L, blobs, int(L.bytes), cfg["act"])
+
+    def step():
+        logits = TS.router_logits_f32(router, x0)
+        ids, w = TS.route_rows(logits, K, 0, cfg["in_scale"], None, escale, True, 0.0)
+        xq = TS.quantize_q8_1_rows(x0)
+        out = ep_forward(xq, ids, w, E, H, fn)
+        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xq, None, cfg["act"])
+        shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
+        return out.add_(shared)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    assert TS.device_error() == 0
+    if rank == 0:
+        ops = prefill_ops(T, H, F, FS, K, E) * ws
+        line = {
+            "metric": EP_METRIC, "value": ws * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_1 x Q4_0 exact block dots on tcgen05, fp32 block scaling",
+            "data": "synthetic",
+            "config": {"workload": f"expert-parallel prefill, {T} tokens per GPU, {per} of {E} experts per GPU",
+                       "tokens_per_gpu": T, "experts_per_gpu": per, "parallelism": f"ep{ws}",
+                       "collectives": "NCCL all_to_all_single (counts, q8_1 rows, picks; fp32 partial rows back)"},
+            "us_per_layer": ms * 1e3,
+            "roofline": {"bound": "tensor", "achieved": ops / (ms * 1e-3) / 1e12 / ws, "unit": "TFLOP/s per GPU",
+                         "note": "int8-op/s, algorithmic"},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -247,13 +329,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
+                    help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192); "
+                         "ep: that layer expert-parallel over the launched ranks")
     args = ap.parse_args()
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "ep"):
         if args.tokens == 1:
             args.tokens = 8192
-        return bench_prefill(args)
+        return bench_prefill(args) if args.workload == "prefill" else bench_ep(args)
     global N_LAYERS
     N_LAYERS = args.layers
     if args.impl == "reference":
