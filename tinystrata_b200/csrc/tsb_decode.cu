@@ -20,18 +20,20 @@ int dfail(int code, const char* fmt, ...) {
     return code;
 }
 
+// Every exchange buffer holds tagged 8-byte words (value, layer + 1); the whole workspace is zeroed before each launch
+// so that no word carries a tag of this launch before it is written.
 struct WsLayout {
-    size_t logits, hsh, hbuf, sh_out, bar, err, total;
+    size_t logits, hsh, hbuf, sh_out, xt, err, total;
 };
 WsLayout ws_layout(const tsb_decode_desc* d) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t) 255; };
     WsLayout w;
     size_t o = 0;
-    w.logits = o; o += al((size_t) d->n_tok * (d->n_expert + 1) * 2 * 4);
-    w.hsh = o;    o += al((size_t) d->n_tok * d->sh_n_ff * 4);
-    w.hbuf = o;   o += al((size_t) d->n_tok * d->n_used * d->n_ff * 4);
-    w.sh_out = o; o += al((size_t) d->n_tok * d->n_embd * 4);
-    w.bar = o;    o += 256;
+    w.logits = o; o += al((size_t) d->n_tok * (d->n_expert + 1) * 2 * 8);
+    w.hsh = o;    o += al((size_t) d->n_tok * d->sh_n_ff * 8);
+    w.hbuf = o;   o += al((size_t) d->n_tok * d->n_used * d->n_ff * 8);
+    w.sh_out = o; o += al((size_t) d->n_tok * d->n_embd * 8);
+    w.xt = o;     o += al((size_t) d->n_tok * d->n_embd * 8);
     w.err = o;    o += 8192;   // error word, its context (words 1..127), one progress word per CTA from word 128
     w.total = o;
     return w;
@@ -60,7 +62,7 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     p.s_up_off = (uint64_t) FS * p.sgu_row;
     p.s_down_off = 2 * p.s_up_off;
     p.R = 4;   // four rows per routed down task: one pass of 32 lanes over their two blocks each (F = 512)
-    p.rt_per_unit = (int) (kSlotBytes / (2 * p.gu_row));
+    p.rt_per_unit = std::min(2, (int) (kSlotBytes / (2 * p.gu_row)));   // two row pairs: units for every warp at T = 1
     p.sd_per_unit = (int) (kSlotBytes / p.sd_row);
     while (p.sd_per_unit > 1 && H % p.sd_per_unit) --p.sd_per_unit;
     // Two routed down tasks (4 rows of one expert each) per slot: about one unit per consumer warp at T = 1.
@@ -68,13 +70,16 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     if (p.gu_row % 16 || p.sgu_row % 16 || p.sd_row % 16 || p.blob_bytes % 16 || p.rt_per_unit < 1 || F % p.rt_per_unit ||
         2 * p.sgu_row > kSlotBytes || p.dn_per_unit < 1 || H % p.R)
         return dfail(TSB_ERR_UNSUPPORTED, "decode: rows do not fit the ring slots");
-    int dev = 0, reserved = 0;
+    int dev = 0, reserved = 0, max_smem = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+    cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     p.smem_base = (uint32_t) reserved;
-    if (p.smem_base + (uint32_t) kSlots * kSlotBytes > 0x10000u)
-        return dfail(TSB_ERR_UNSUPPORTED, "decode: %d reserved bytes leave no room for the ring", reserved);
-    smem = dec_smem(p.smem_base, T, H, F, FS, K).total;
+    if (p.smem_base + (uint32_t) (2 * kLowWarps) * kSlotBytes > 0x10000u || (uint32_t) kDecWarps * kSlotBytes > 2 * kLowWarps * kSlotBytes)
+        return dfail(TSB_ERR_UNSUPPORTED, "decode: %d reserved bytes leave no room for the slots", reserved);
+    // two slots a warp (a unit in flight ahead of the one computing) when shared memory allows, else one
+    p.nslot = dec_smem(p.smem_base, T, H, F, FS, K, 2).total <= (uint32_t) max_smem ? 2 : 1;
+    smem = dec_smem(p.smem_base, T, H, F, FS, K, p.nslot).total;
     return TSB_OK;
 }
 
@@ -108,14 +113,16 @@ int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* laye
     if (!coop) return dfail(TSB_ERR_UNSUPPORTED, "decode: device without cooperative launch");
     if ((int) smem > max_smem) return dfail(TSB_ERR_UNSUPPORTED, "decode: %zu bytes of shared memory > %d", smem, max_smem);
     if ((p.H / p.R + sms - 1) / sms * p.R > kDecMaxRows) return dfail(TSB_ERR_UNSUPPORTED, "decode: too few SMs");
+    // every CTA computes some of P1 (router or shared gate/up rows): the reuse of the exchange buffers relies on it
+    if (2 * (p.E + 1) + p.FS < sms) return dfail(TSB_ERR_UNSUPPORTED, "decode: fewer P1 rows than SMs");
     uint8_t* ws = (uint8_t*) workspace;
     p.layers = (const DecLayer*) layers;
     p.x = x;
-    p.logits = (float*) (ws + w.logits);
-    p.hsh = (float*) (ws + w.hsh);
-    p.hbuf = (float*) (ws + w.hbuf);
-    p.sh_out = (float*) (ws + w.sh_out);
-    p.bar = (unsigned*) (ws + w.bar);
+    p.logits = (uint64_t*) (ws + w.logits);
+    p.hsh = (uint64_t*) (ws + w.hsh);
+    p.hbuf = (uint64_t*) (ws + w.hbuf);
+    p.sh_out = (uint64_t*) (ws + w.sh_out);
+    p.xt = (uint64_t*) (ws + w.xt);
     p.err = (unsigned*) (ws + w.err);
     p.ids_rec = ids_rec;
     p.w_rec = w_rec;
@@ -125,7 +132,7 @@ int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* laye
     auto kern = k_decode_layers<8>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) != cudaSuccess)
         return dfail(TSB_ERR_CUDA, "decode: shared memory attribute: %s", cudaGetErrorString(cudaGetLastError()));
-    if (cudaMemsetAsync(ws + w.bar, 0, w.total - w.bar, s) != cudaSuccess)
+    if (cudaMemsetAsync(ws, 0, w.total, s) != cudaSuccess)
         return dfail(TSB_ERR_CUDA, "decode: memset: %s", cudaGetErrorString(cudaGetLastError()));
     void* args[] = {&p};
     const cudaError_t e = cudaLaunchCooperativeKernel((const void*) kern, dim3(sms), dim3(kDecThreads), args, smem, s);

@@ -1,22 +1,31 @@
 // tsb_decode.cuh - the whole decode MoE block of every layer of a step in ONE persistent kernel.
 //
 // Per layer (the reference's call stack A, src/qwen35/q36_engine.cu:2821-2925, with k_moe_out_small's epilogue):
-//   P0  every CTA: h = rms(x) (the 256-slot order of q36_kernels.cuh:252-290) and its q8_1 image in shared memory
+//   P0  every CTA: x (the previous layer's rows from every CTA), h = rms(x) (the 256-slot order of
+//       q36_kernels.cuh:252-290) and its q8_1 image in shared memory
 //   P1  router logits (fp32 rows, the shared-gate row appended) and the shared expert's gate/up + SwiGLU
-//   --- grid barrier
-//   R   every CTA: softmax top-k of every token (native_router.cu:44-95) and the grouping (q36_engine.cu:396-422)
+//   R   every CTA: softmax top-k of every token (native_router.cu:44-95) once the logits of every CTA are in, the
+//       grouping (q36_engine.cu:396-422), then the shared hidden vector into q8_1
 //   P2  routed experts' gate/up + SwiGLU (IQ3_XXS), the shared expert's down rows (Q8_0)
-//   --- grid barrier
-//   P3  routed down rows of this CTA's row chunks for every group, then the combine of those rows:
-//       x += sum_k w_k part_k (fma in pick order) + sigmoid(gate) shared
-//   --- grid barrier
+//   P3  the routed hidden vectors of every CTA into q8_1, routed down rows of this CTA's row chunks for every group,
+//       then the combine of those rows: x += sum_k w_k part_k (fma in pick order) + sigmoid(gate) shared
 //
-// One CTA per SM (cooperative launch), 16 warps: warp 15 lane 0 is the producer, streaming every unit of work's weight
-// bytes with cp.async.bulk into a ring of shared-memory slots (full / empty mbarriers per slot) as far ahead as the
-// ring allows: the next phase's bytes (and the next layer's router and shared-expert rows) are in flight while this
-// phase computes and while the grid barriers wait.  Warps 0-14 consume units in order, claiming them from a counter.
-// Every wait is bounded (2 s of %globaltimer); a wait that gives up records its site in the error word and the kernel
-// winds down.
+// No grid-wide barrier: every value one CTA hands to others (logits, hidden vectors, shared output, x) travels as a
+// tagged 8-byte word (value, layer + 1) and the readers poll the words they need until the tags are the layer's, so a
+// phase waits one L2 round trip for its slowest input instead of a barrier's arrive + release.  The dependencies order
+// the reuse of every buffer: a CTA overwrites a word of layer l only after reading inputs that every CTA produced after
+// it had read that word (P1 of l + 1 needs every CTA's x of l, which follows their P3 of l; P2 of l + 1 needs every
+// CTA's shared hidden of l + 1, which follows their P0 of l + 1; P3 of l + 1 writes x after every CTA's P1 of l + 1).
+//
+// One CTA per SM (cooperative launch: every CTA resident), 12 warps (three per SM sub-partition: 168 registers a
+// thread, no spills).  Every warp streams its own units of weight bytes: unit j of a phase goes to warp j mod 12, and
+// lane 0 issues the unit's cp.async.bulk copies into one of the warp's two shared-memory slots, completing on that
+// slot's mbarrier, two units ahead of the warp's compute.  The stream runs across phases -- the first routed-down
+// rows are in flight while the last gate/up rows compute, the next layer's router and shared-expert rows while this
+// layer's down rows compute -- and no warp waits for another to move its data (a single producer warp, tried first,
+// was starved of issue slots by the compute warps sharing its sub-partition).  Every wait is bounded (2 s of
+// %globaltimer); a wait that gives up records its site in the error word, the other CTAs see the word and the
+// kernel winds down.
 #pragma once
 
 #include "tsb_kernels.cuh"
@@ -25,9 +34,9 @@
 
 namespace tsb {
 
-constexpr int kDecWarps = 16, kDecConsumers = 15, kDecThreads = kDecWarps * 32, kDecCThreads = kDecConsumers * 32;
-constexpr int kSlots = 14;   // 14 x 4352 bytes below the tables (which sit at shared address 0x10000)
-constexpr uint32_t kSlotBytes = 4352;
+constexpr int kDecWarps = 12, kDecConsumers = kDecWarps, kDecThreads = kDecWarps * 32, kDecCThreads = kDecThreads;
+constexpr uint32_t kSlotBytes = 4352;   // the largest unit: a shared gate/up row pair, 8 shared down rows
+constexpr int kLowWarps = 7;            // warps whose two slots sit below the tables (7 x 2 x 4352 bytes)
 constexpr int kDecMaxT = 16, kDecMaxEnt = 128, kDecMaxRows = 16;   // rows of H per CTA in P3 (<= 4 chunks of 4)
 
 struct DecLayer {
@@ -41,16 +50,18 @@ struct DecParams {
     uint32_t gu_row, d_row, sgu_row, sd_row;
     uint64_t up_off, down_off, blob_bytes, s_up_off, s_down_off;
     int R;                    // routed down rows per chunk (R * d_row % 16 == 0)
-    int rt_per_unit, sd_per_unit, dn_per_unit;   // items packed per ring slot
+    int rt_per_unit, sd_per_unit, dn_per_unit;   // items packed per unit (one slot)
+    int nslot;                // slots per warp: 2 (prefetch a unit ahead), 1 when shared memory is short (large T)
     const DecLayer* layers;
     float* x;                 // [T][H] residual stream, in / out
-    float* logits;            // [T][E + 1][2]: the two half-row partial dots
-    float* hsh;               // [T][FS] shared hidden
-    float* hbuf;              // [T * K][F] routed hidden, by entry
-    float* sh_out;            // [T][H] shared expert output
+    // tagged words (value, layer + 1), zero at launch
+    uint64_t* logits;         // [T][E + 1][2]: the two half-row partial dots
+    uint64_t* hsh;            // [T][FS] shared hidden
+    uint64_t* hbuf;           // [T * K][F] routed hidden, by entry
+    uint64_t* sh_out;         // [T][H] shared expert output
+    uint64_t* xt;             // [T][H] the residual stream after each layer
     int32_t* ids_rec;         // [layers][T][K] or null
     float* w_rec;
-    unsigned* bar;            // grid barrier counter (zero at launch)
     unsigned* err;
     unsigned long long* trace;   // optional phase stamps: [layer][kTraceEvents][CTA] of %globaltimer, or null
     float eps;
@@ -59,16 +70,8 @@ struct DecParams {
 constexpr int kTraceEvents = 16;
 
 struct DecShared {
-    uint64_t full[kSlots], empty[kSlots], route;
-    int claim;
-    int abort;
-    volatile int prod_seq, prod_state;   // the producer's progress (diagnostics of a wait that gives up)
-    volatile int warp_unit[kDecConsumers];   // the ring sequence each consumer warp waits on or works on
-    volatile int warp_state[kDecConsumers];  // 1 waiting, 2 computing, 3 released
-    // The ring lap the producer has started on each slot.  A consumer may claim a unit a whole lap ahead of a slot's
-    // previous unit; waiting on the full barrier's parity is only unambiguous once the producer has started that lap
-    // (a barrier still in phase lap - 1 answers a wait on parity lap & 1 as complete: the preceding phase).
-    volatile int slot_lap[kSlots];
+    uint64_t bar[kDecWarps][2];   // per warp and slot: the bulk copies of the unit in the slot have landed
+    volatile int abort;
     unsigned canary;
     int n_groups;
     float rms[kDecMaxT];
@@ -77,18 +80,20 @@ struct DecShared {
     float w[kDecMaxEnt];
     int32_t grp_expert[kDecMaxEnt], grp_start[kDecMaxEnt + 1], ent_dst[kDecMaxEnt], ent_tok[kDecMaxEnt];
     float red[256];
+    float xown[kDecMaxT][kDecMaxRows];   // this CTA's rows of x (it is their only writer)
 };
 
-// Offsets inside the dynamic shared memory (dynamic base at shared address b0 <= 0x10000 - kSlots * kSlotBytes):
-//   [0, kSlots * kSlotBytes)              the ring
+// Offsets inside the dynamic shared memory (dynamic base at shared address b0 <= 0x10000 - 14 * kSlotBytes):
+//   [0, 14 * kSlotBytes)                  warps 0..6's two slots each (nslot 2), or every warp's one slot (nslot 1)
 //   [0x10000 - b0, +64 KB)                the IQ3_XXS tables at shared address 0x10000
 //   [0x20000 - b0, ...)                   DecShared, parts [kDecMaxEnt][kDecMaxRows], then the activation union:
 //       P0..P2: xq codes [T][H], xq scales [T][H / 32], hshq codes [T][FS], hshq scales [T][FS / 32]
 //       P3:     hq codes [T K][F], hq scales [T K][F / 32]
+//   then (nslot 2) warps 7..11's two slots each
 struct DecSmem {
-    uint32_t tab, shared, parts, uni, xq_d, hs, hs_d, hq_d, total;
+    uint32_t tab, shared, parts, uni, xq_d, hs, hs_d, hq_d, slots_hi, total;
 };
-__host__ __device__ inline DecSmem dec_smem(uint32_t b0, int T, int H, int F, int FS, int K) {
+__host__ __device__ inline DecSmem dec_smem(uint32_t b0, int T, int H, int F, int FS, int K, int nslot) {
     auto al = [](uint32_t v, uint32_t a) { return (v + a - 1) / a * a; };
     DecSmem m;
     m.tab = 0x10000u - b0;
@@ -101,8 +106,14 @@ __host__ __device__ inline DecSmem dec_smem(uint32_t b0, int T, int H, int F, in
     const uint32_t end1 = m.hs_d + (uint32_t) (T * (FS / 32) * 4);
     m.hq_d = m.uni + (uint32_t) (T * K * F);
     const uint32_t end2 = m.hq_d + (uint32_t) (T * K * (F / 32) * 4);
-    m.total = end1 > end2 ? end1 : end2;
+    m.slots_hi = al(end1 > end2 ? end1 : end2, 128);
+    m.total = m.slots_hi + (nslot == 2 ? (uint32_t) (kDecWarps - kLowWarps) * 2 * kSlotBytes : 0u);
     return m;
+}
+// The shared-memory offset of slot s of warp w.
+__device__ __forceinline__ uint32_t slot_offset(const DecSmem& m, int nslot, int w, int s) {
+    if (nslot == 1) return (uint32_t) w * kSlotBytes;
+    return w < kLowWarps ? (uint32_t) (2 * w + s) * kSlotBytes : m.slots_hi + (uint32_t) (2 * (w - kLowWarps) + s) * kSlotBytes;
 }
 
 // -------------------------------------------------------------------------------------------------- small helpers
@@ -117,45 +128,75 @@ __device__ __forceinline__ void report_detail(unsigned* err, unsigned site, unsi
         __threadfence();
     }
 }
-// Phase stamps (consumers: 0 layer start, 1 P0, 2 P1, 3 barrier, 4 routing, 5 P2, 6 barrier, 7 P3 + combine,
-// 8 barrier; producer: 9 P1 issued, 10 routing seen, 11 P2 issued, 12 P3 issued).
+// Phase stamps of thread 0: 0 layer start, 1 P0, 2 P1, 3 routed, 4 shared hidden quantised, 5 P2, 6 routed hidden
+// quantised, 7 P3 + combine, 8 layer end.
 __device__ __forceinline__ void stamp(const DecParams& p, int l, int ev) {
     if (p.trace) p.trace[((size_t) l * kTraceEvents + ev) * gridDim.x + blockIdx.x] = globaltimer();
     if (ev < 9) ((volatile unsigned*) p.err)[128 + blockIdx.x] = ((unsigned) l << 8) | (unsigned) ev;
 }
 __device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// A named barrier that also ORs one flag over its threads: every thread gets the same verdict, whatever another thread
+// writes to the flag's source after the barrier -- the warps leave the layer loop together.
+__device__ __forceinline__ bool named_sync_or(int id, int n, int flag) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"(flag), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Consumers: all 480 threads.  Thread 0 publishes this CTA's arrival and waits for the others (acquire), bounded.
-__device__ bool grid_barrier(const DecParams& p, DecShared& S, unsigned& target, unsigned site) {
-    named_sync(1, kDecCThreads);
-    target += gridDim.x;
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(p.bar, 1u);
+// One pass of a poll found a word not yet written: poll again (no sleep: __nanosleep measured here oversleeps by
+// microseconds, and a pass is an L2 round trip already), or give up after the bound or when another CTA has recorded
+// an error (then this CTA winds down too).  Returns true when the caller must stop waiting.
+__device__ __forceinline__ bool poll_give_up(const DecParams& p, DecShared& S, uint64_t t0, unsigned site) {
+    if (S.abort || *(volatile unsigned*) p.err != 0u || globaltimer() - t0 > kWaitNs) {
+        report_error(p.err, site);
+        S.abort = 1;
+        return true;
+    }
+    return false;
+}
+
+// n tagged words (n even, 16-byte aligned) into floats in shared memory once all carry `tag`; threads tid of nth,
+// up to 8 words of a thread in flight per pass.  false: gave up (S.abort set).
+__device__ bool poll_copy(const DecParams& p, DecShared& S, const uint64_t* src, int n, uint32_t tag, float* dst,
+                          int tid, int nth, unsigned site) {
+    const int np = n / 2;
+    for (int base = tid; base < np; base += 4 * nth) {
         const uint64_t t0 = globaltimer();
-        unsigned v;
-        while ((v = ld_acquire(p.bar)) < target) {
-            if (globaltimer() - t0 > kWaitNs || S.abort) {
-                report_error(p.err, site);
-                if (p.err && atomicCAS(p.err + 99, 0u, 1u) == 0u) {
-                    p.err[100] = site;
-                    p.err[101] = v;
-                    p.err[102] = target;
-                    p.err[103] = (unsigned) S.prod_state;
-                    p.err[104] = blockIdx.x;
+        for (;;) {
+            uint64_t w[8];
+            bool ok = true;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = base + j * nth;
+                if (i < np) {
+                    ld_tag2(src + 2 * i, w[2 * j], w[2 * j + 1]);
+                    ok &= tag_is(w[2 * j], tag) & tag_is(w[2 * j + 1], tag);
                 }
-                S.abort = 1;
+            }
+            if (ok) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int i = base + j * nth;
+                    if (i < np) {
+                        dst[2 * i] = tag_val(w[2 * j]);
+                        dst[2 * i + 1] = tag_val(w[2 * j + 1]);
+                    }
+                }
                 break;
             }
+            if (poll_give_up(p, S, t0, site)) return false;
         }
     }
-    named_sync(1, kDecCThreads);
-    return !S.abort;
+    return true;
 }
 
 // -------------------------------------------------------------------------------------------------- unit lists
@@ -170,83 +211,103 @@ __device__ __forceinline__ int p1_units(const DecParams& p) { return 2 * (p.E + 
 __device__ __forceinline__ int p2_rt_units(const DecParams& p, int ng) { return (ng * p.F + p.rt_per_unit - 1) / p.rt_per_unit; }
 __device__ __forceinline__ int p2_units(const DecParams& p, int ng) { return p2_rt_units(p, ng) + p.H / p.sd_per_unit; }
 __device__ __forceinline__ Range my_chunks(const DecParams& p) { return split(p.H / p.R, gridDim.x, blockIdx.x); }
+// Units [0, n) are dealt to the warps round robin: how many warp w gets.
+__device__ __forceinline__ int per_warp(int n, int w) { return n > w ? (n - w + kDecWarps - 1) / kDecWarps : 0; }
 __device__ __forceinline__ int p3_units(const DecParams& p, int ng) {
     const Range c = my_chunks(p);
     return ((c.hi - c.lo) * ng + p.dn_per_unit - 1) / p.dn_per_unit;
 }
 
-// -------------------------------------------------------------------------------------------------- producer
+// -------------------------------------------------------------------------------------------------- unit copies
 struct BulkCopy {
     const void* src;
     uint32_t dst;     // offset in the slot
     uint32_t bytes;
 };
-
-struct Producer {
-    uint32_t seq = 0;   // ring sequence number of the next unit (identical in every lane of the producer warp)
-    uint8_t* ring;
-    DecShared* S;
-    const DecParams* p;
-
-    __device__ uint8_t* slot_ptr(uint32_t slot) const { return ring + (size_t) slot * kSlotBytes; }
-    // Is the slot of sequence number s free (its previous lap released by the consumers)?  wait: bounded wait.
-    __device__ bool slot_free(uint32_t s, bool wait) {
-        if (s < (uint32_t) kSlots) return true;
-        const uint32_t slot = s % kSlots, par = ((s / kSlots) - 1) & 1u;
-        if (!wait) return mbar_test_wait(&S->empty[slot], par);
-        if (mbar_try_wait(&S->empty[slot], par)) return true;
-        const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(&S->empty[slot], par)) {
-            if (globaltimer() - t0 > kWaitNs || S->abort) {
-                report_detail(p->err, 0x310u, s, (unsigned) S->prod_state, (unsigned) S->claim, blockIdx.x);
-                S->abort = 1;
-                return false;
-            }
-        }
-        return true;
+// P1 unit u: a router half row (one copy) or a shared gate/up row pair (two).
+__device__ __forceinline__ int p1_copies(const DecParams& p, const DecLayer& L, int u, BulkCopy (&c)[2]) {
+    const int nrh = 2 * (p.E + 1);
+    if (u < nrh) {
+        const int o = u >> 1, half = u & 1;
+        c[0] = {L.router + (size_t) o * p.H + half * (p.H / 2), 0u, (uint32_t) (p.H / 2 * 4)};
+        return 1;
     }
-    // Units [lo, hi) of a phase.  copies(u): bulk copies of unit u (<= 32 over a batch); bytes(u): their total;
-    // copy(u, c): copy c of unit u (source, offset in the slot, bytes).  Lane 0 takes the next slot (waiting) and the
-    // free ones after it; lane j starts unit j of the batch (publishes its lap, arms its barrier); then every lane
-    // issues its copy in ONE converged instruction (a cp.async.bulk issued under divergence goes out lane by lane,
-    // each holding the warp for a fraction of a memory latency).
-    template <class NC, class NB, class CP>
-    __device__ bool produce(int lo, int hi, NC copies, NB bytes, CP copy) {
-        const int lane = threadIdx.x & 31;
-        for (int u = lo; u < hi;) {
-            int nb = 0;
-            if (lane == 0 && slot_free(seq, true)) {
-                int ncp = copies(u);
-                nb = 1;
-                while (u + nb < hi && nb < kSlots && ncp + copies(u + nb) <= 32 && slot_free(seq + nb, false))
-                    ncp += copies(u + nb++);
-            }
-            nb = __shfl_sync(0xffffffffu, nb, 0);
-            if (nb == 0) return false;
-            if (lane < nb) {
-                const uint32_t s = seq + lane, slot = s % kSlots;
-                S->slot_lap[slot] = (int) (s / kSlots);
-                mbar_expect_tx(&S->full[slot], bytes(u + lane));
-            }
-            __syncwarp();
-            int mj = -1, mc = 0, base = 0;
-            for (int j = 0; j < nb; ++j) {
-                const int n = copies(u + j);
-                if (lane >= base && lane < base + n) {
-                    mj = j;
-                    mc = lane - base;
-                }
-                base += n;
-            }
-            const BulkCopy cp = copy(u + max(mj, 0), mc);
-            const uint32_t slot = (seq + (uint32_t) max(mj, 0)) % kSlots;
-            if (mj >= 0) bulk_g2s(slot_ptr(slot) + cp.dst, cp.src, cp.bytes, &S->full[slot]);
-            __syncwarp();
-            seq += (uint32_t) nb;
-            u += nb;
-            if (lane == 0) S->prod_seq = (int) seq;
+    const size_t off = (size_t) (u - nrh) * p.sgu_row;
+    c[0] = {L.sh_blob + off, 0u, p.sgu_row};
+    c[1] = {L.sh_blob + off + p.s_up_off, p.sgu_row, p.sgu_row};
+    return 2;
+}
+// P2 unit u: rt_per_unit routed gate rows then the same up rows (two copies, one expert), or sd_per_unit shared down rows.
+__device__ __forceinline__ int p2_copies(const DecParams& p, const DecLayer& L, const DecShared& S, int ng, int u,
+                                         BulkCopy (&c)[2]) {
+    const int nrt = p2_rt_units(p, ng);
+    if (u < nrt) {
+        const int i0 = u * p.rt_per_unit, n = min(p.rt_per_unit, ng * p.F - i0);
+        const int g = i0 / p.F, r = i0 % p.F;
+        const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + (size_t) r * p.gu_row;
+        c[0] = {b, 0u, (uint32_t) n * p.gu_row};
+        c[1] = {b + p.up_off, (uint32_t) n * p.gu_row, (uint32_t) n * p.gu_row};
+        return 2;
+    }
+    const int r0 = (u - nrt) * p.sd_per_unit;
+    c[0] = {L.sh_blob + p.s_down_off + (size_t) r0 * p.sd_row, 0u, (uint32_t) p.sd_per_unit * p.sd_row};
+    return 1;
+}
+// P3 unit k: this CTA's tasks [k dn, (k + 1) dn) (task i = chunk i % nch of group i / nch): one copy per group touched.
+__device__ __forceinline__ int p3_copies(const DecParams& p, const DecLayer& L, const DecShared& S, int ng, Range ch,
+                                         int k, BulkCopy (&c)[2]) {
+    const int nch = ch.hi - ch.lo, ntask = nch * ng;
+    const uint32_t cb = (uint32_t) p.R * p.d_row;
+    const int i0 = k * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
+    int n = 0;
+    for (int g = i0 / nch; g <= (i1 - 1) / nch && n < 2; ++g) {
+        const int a0 = max(i0, g * nch), a1 = min(i1, (g + 1) * nch);
+        c[n++] = {L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + p.down_off + (size_t) (ch.lo + a0 - g * nch) * cb,
+                  (uint32_t) (a0 - i0) * cb, (uint32_t) (a1 - a0) * cb};
+    }
+    return n;
+}
+
+// One warp's stream of units through its slots: issue (lane 0: expect the unit's bytes on the slot's barrier, then
+// its bulk copies), wait (every lane observes the slot's phase), release.  Units are consumed in the order issued.
+struct WarpStream {
+    uint32_t slot[2];   // shared addresses
+    uint64_t* bar;      // the warp's two barriers
+    uint32_t issued = 0, consumed = 0;
+    int nslot;
+    __device__ bool can_issue() const { return issued - consumed < (uint32_t) nslot; }
+    __device__ void issue(const BulkCopy (&c)[2], int n, int lane) {
+        const uint32_t k = issued % (uint32_t) nslot;
+        if (lane == 0) {
+            uint32_t bytes = 0;
+            for (int i = 0; i < n; ++i) bytes += c[i].bytes;
+            mbar_expect_tx(&bar[k], bytes);
+            for (int i = 0; i < n; ++i)
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                 slot[k] + c[i].dst),
+                             "l"(c[i].src), "r"(c[i].bytes), "r"(smem_u32(&bar[k]))
+                             : "memory");
         }
-        return true;
+        ++issued;
+    }
+    // The next unit's bytes (generic pointer into the dynamic shared memory at smem_ptr / smem_base), or null when the
+    // wait gave up.
+    __device__ const uint8_t* wait(uint8_t* smem_ptr, uint32_t smem_base) {
+        const uint32_t k = consumed % (uint32_t) nslot, par = (consumed / (uint32_t) nslot) & 1u;
+        bool done = mbar_try_wait(&bar[k], par);
+        const uint64_t t0 = done ? 0 : globaltimer();
+        while (!done) {
+            done = mbar_try_wait(&bar[k], par);
+            if (!done && globaltimer() - t0 > kWaitNs) break;
+        }
+        if (!__all_sync(0xffffffffu, done)) return nullptr;
+        return smem_ptr + (slot[k] - smem_base);
+    }
+    // The warp has read the slot: order those reads before the next bulk copy into it (async proxy).
+    __device__ void release() {
+        fence_proxy_async();
+        __syncwarp();
+        ++consumed;
     }
 };
 
@@ -266,6 +327,7 @@ struct XqView {
         return r;
     }
 };
+
 
 // Rows of fp32 (written by other CTAs of this launch) into a q8_1 image in shared memory: one warp per 32-value block,
 // the reference's quantiser (the same bits as q8_1_lane / the standalone kernel).
@@ -324,6 +386,66 @@ __device__ __forceinline__ void quantize_blocks(const float* src, int n, int8_t*
     }
 }
 
+// quantize_blocks over tagged words written by other CTAs of this launch: each pass loads a lane's 2 x 4 words and
+// polls until their tags are `tag` (the lanes of a block rejoin before its shuffles).  false: gave up (S.abort set).
+__device__ bool quantize_tagged(const DecParams& p, DecShared& S, const uint64_t* src, int n, uint32_t tag,
+                                int8_t* codes, float* dsc, int warp, int lane, int nwarps, unsigned site) {
+    const int n4 = n / 4;
+    const int stride = nwarps * 32;
+    bool good = true;
+    for (int base = warp * 32 + lane; base - lane < n4; base += 2 * stride) {
+        float4 v[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+        const uint64_t t0 = globaltimer();
+        while (good) {
+            uint64_t w[8];
+            bool ok = true;
+#pragma unroll
+            for (int it = 0; it < 2; ++it) {
+                const int i = base + it * stride;
+                if (i < n4) {
+                    ld_tag2(src + 4 * i, w[4 * it], w[4 * it + 1]);
+                    ld_tag2(src + 4 * i + 2, w[4 * it + 2], w[4 * it + 3]);
+                    ok &= tag_is(w[4 * it], tag) & tag_is(w[4 * it + 1], tag) & tag_is(w[4 * it + 2], tag) &
+                          tag_is(w[4 * it + 3], tag);
+                }
+            }
+            if (ok) {
+#pragma unroll
+                for (int it = 0; it < 2; ++it)
+                    v[it] = make_float4(tag_val(w[4 * it]), tag_val(w[4 * it + 1]), tag_val(w[4 * it + 2]),
+                                        tag_val(w[4 * it + 3]));
+                break;
+            }
+            if (poll_give_up(p, S, t0, site)) good = false;
+        }
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+            const int i = base + it * stride;
+            if (i - lane >= n4) break;   // warp-uniform: whole warps of 4-value groups
+            float amax = fmaxf(fmaxf(fabsf(v[it].x), fabsf(v[it].y)), fmaxf(fabsf(v[it].z), fabsf(v[it].w)));
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float d = q8_finite(fdiv_fm(amax, 127.0f));
+            uint32_t word = 0;
+            const float xs[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int8_t c = 0;
+                if (amax != 0.0f) {
+                    const float r = roundf(fdiv_fm(xs[j], d));
+                    c = (int8_t) (r > 127.0f ? 127.0f : r < -127.0f ? -127.0f : r);
+                }
+                word |= (uint32_t) (uint8_t) c << (8 * j);
+            }
+            if (i < n4) {
+                ((uint32_t*) codes)[i] = word;
+                if ((lane & 7) == 0) dsc[i >> 3] = __half2float(__float2half(d));
+            }
+        }
+    }
+    return good;
+}
+
 // IQ3_XXS gate/up row of 8 blocks (H = 2048) against one activation, with the block parity uniform per step: lane
 // l = 8 q + c decodes call c of block 2 q (step 0, 4-byte aligned) and of block 2 q + 1 (step 1, 2 mod 4); a[j] is the
 // q8_1 block of that call (iq3_par_call).  The sum has the bits of the reference's row order -- lane L adds call L's
@@ -377,10 +499,8 @@ __device__ __forceinline__ void iq3_row(const uint8_t* row, int C, int lane, con
 template <int V>   // V = E / 32 router values per lane
 __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const DecSmem M = dec_smem(p.smem_base, p.T, p.H, p.F, p.FS, p.K);
-    uint8_t* ring = smem;
-    uint8_t* tab = smem + M.tab;
-    DecShared& S = *(DecShared*) (smem + M.shared);
+    DecShared& S = *(DecShared*) (smem + (0x20000u - p.smem_base));
+    const DecSmem M = dec_smem(p.smem_base, p.T, p.H, p.F, p.FS, p.K, p.nslot);
     float* parts = (float*) (smem + M.parts);
     int8_t* xq_codes = (int8_t*) (smem + M.uni);
     float* xq_d = (float*) (smem + M.xq_d);
@@ -395,234 +515,80 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         return;
     }
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kSlots; ++s) {
-            mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], 1);
+        for (int w = 0; w < kDecWarps; ++w) {
+            mbar_init(&S.bar[w][0], 1);
+            mbar_init(&S.bar[w][1], 1);
         }
-        mbar_init(&S.route, 1);
-        S.claim = 0;
         S.abort = 0;
-        S.prod_seq = 0;
-        S.prod_state = 0;
         S.canary = 0xC0FFEE01u;
-        for (int q = 0; q < kSlots; ++q) S.slot_lap[q] = -1;
         if (blockIdx.x == 0 && p.err) {   // the layout as the device sees it
             p.err[110] = smem_u32(smem);
-            p.err[111] = smem_u32(tab);
+            p.err[111] = M.tab;
             p.err[112] = smem_u32(&S);
-            p.err[113] = smem_u32(parts);
-            p.err[114] = smem_u32(xq_codes);
+            p.err[113] = M.parts;
+            p.err[114] = M.uni;
             p.err[115] = M.total;
         }
         fence_mbar_init();
     }
+    fill_tables<T_IQ3_XXS>(smem + (0x10000u - p.smem_base), kDecThreads);
     __syncthreads();
-
-    // ============================================================================================ producer
-    // The whole warp: lane 0 takes free ring slots in order, then the lanes issue the batch's bulk copies side by side
-    // (one thread's cp.async.bulk issues serialise at a memory latency's fraction each; 32 lanes overlap them).
-    if (warp == kDecWarps - 1) {
-        Producer pr;
-        pr.ring = ring;
-        pr.S = &S;
-        pr.p = &p;
-        for (int l = 0; l < p.n_layers && !S.abort; ++l) {
-            const DecLayer L = p.layers[l];
-            if (lane == 0) S.prod_state = (l << 4) | 1;
-            // P1: router half rows (one copy), shared gate/up row pairs (two)
-            const Range r1 = split(p1_units(p), gridDim.x, blockIdx.x);
-            const int nrh = 2 * (p.E + 1);
-            auto p1_copies = [&](int u) { return u < nrh ? 1 : 2; };
-            auto p1_bytes = [&](int u) { return u < nrh ? (uint32_t) (p.H / 2 * 4) : 2 * p.sgu_row; };
-            auto p1_copy = [&](int u, int c) -> BulkCopy {
-                if (u < nrh) {
-                    const int o = u >> 1, half = u & 1;
-                    return {L.router + (size_t) o * p.H + half * (p.H / 2), 0u, (uint32_t) (p.H / 2 * 4)};
-                }
-                const size_t off = (size_t) (u - nrh) * p.sgu_row + (c ? p.s_up_off : 0);
-                return {L.sh_blob + off, c * p.sgu_row, p.sgu_row};
-            };
-            if (!pr.produce(r1.lo, r1.hi, p1_copies, p1_bytes, p1_copy)) break;
-            if (lane == 0) stamp(p, l, 9);
-            if (lane == 0) S.prod_state = (l << 4) | 2;
-            {   // this layer's routing (lane 0 waits; the warp barrier orders the routing tables for the other lanes)
-                int ok = 1;
-                if (lane == 0) {
-                    const uint64_t t0 = globaltimer();
-                    while (!mbar_try_wait(&S.route, (uint32_t) (l & 1))) {
-                        if (globaltimer() - t0 > kWaitNs || S.abort) {
-                            report_error(p.err, 0x320u);
-                            S.abort = 1;
-                            break;
-                        }
-                    }
-                    ok = !S.abort;
-                }
-                __syncwarp();
-                if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-            }
-            const int ng = S.n_groups;
-            if (lane == 0) stamp(p, l, 10);
-            if (lane == 0) S.prod_state = (l << 4) | 3 | (ng << 16);
-            // P2: routed gate/up rows (rt_per_unit consecutive rows of one expert: the gate block, then the up block),
-            // then shared down rows (sd_per_unit consecutive rows, one copy)
-            const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
-            const Range r2 = split(n2, gridDim.x, blockIdx.x);
-            auto p2_copies = [&](int u) { return u < nrt ? 2 : 1; };
-            auto p2_bytes = [&](int u) {
-                return u < nrt ? (uint32_t) (min(p.rt_per_unit, ng * p.F - u * p.rt_per_unit) * 2 * p.gu_row)
-                               : (uint32_t) p.sd_per_unit * p.sd_row;
-            };
-            auto p2_copy = [&](int u, int c) -> BulkCopy {
-                if (u < nrt) {
-                    const int i0 = u * p.rt_per_unit, n = min(p.rt_per_unit, ng * p.F - i0);
-                    const int g = i0 / p.F, r = i0 % p.F;
-                    const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + (size_t) r * p.gu_row;
-                    return {b + (c ? p.up_off : 0), (uint32_t) (c * n) * p.gu_row, (uint32_t) n * p.gu_row};
-                }
-                const int r0 = (u - nrt) * p.sd_per_unit;
-                return {L.sh_blob + p.s_down_off + (size_t) r0 * p.sd_row, 0u, (uint32_t) p.sd_per_unit * p.sd_row};
-            };
-            if (!pr.produce(r2.lo, r2.hi, p2_copies, p2_bytes, p2_copy)) break;
-            if (lane == 0) stamp(p, l, 11);
-            if (lane == 0) S.prod_state = (l << 4) | 4 | (ng << 16);
-            // P3: this CTA's down rows of each group, task i = (group i / nch, chunk i % nch): a unit's tasks of one
-            // group are consecutive rows, one copy per group it touches
-            const Range ch = my_chunks(p);
-            const int nch = ch.hi - ch.lo, ntask = nch * ng;
-            const uint32_t cb = (uint32_t) p.R * p.d_row;
-            auto p3_copies = [&](int u) {
-                const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
-                return (i1 - 1) / nch - i0 / nch + 1;
-            };
-            auto p3_bytes = [&](int u) {
-                const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
-                return (uint32_t) (i1 - i0) * cb;
-            };
-            auto p3_copy = [&](int u, int c) -> BulkCopy {
-                const int i0 = u * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
-                const int g = i0 / nch + c;
-                const int a0 = max(i0, g * nch), a1 = min(i1, (g + 1) * nch);
-                const uint8_t* b = L.blobs + (size_t) S.grp_expert[g] * p.blob_bytes + p.down_off +
-                                   (size_t) (ch.lo + a0 - g * nch) * cb;
-                return {b, (uint32_t) (a0 - i0) * cb, (uint32_t) (a1 - a0) * cb};
-            };
-            if (!pr.produce(0, p3_units(p, ng), p3_copies, p3_bytes, p3_copy)) break;
-            if (lane == 0) stamp(p, l, 12);
-        }
-        // wind down: every copy issued is complete before the CTA may exit (bounded)
-        if (lane == 0)
-            for (uint32_t s = pr.seq > kSlots ? pr.seq - kSlots : 0; s < pr.seq; ++s) {
-                const uint64_t t0 = globaltimer();
-                while (!mbar_try_wait(&S.full[s % kSlots], (s / kSlots) & 1u))
-                    if (globaltimer() - t0 > kWaitNs) break;
-            }
-        return;
-    }
-
-    // ============================================================================================ consumers
-    fill_tables<T_IQ3_XXS>(tab, kDecCThreads);   // consumers only, so a named barrier (not __syncthreads)
-    named_sync(1, kDecCThreads);
     if (threadIdx.x == 0 && S.canary != 0xC0FFEE01u) {
         report_error(p.err, 0x3F0u);
         if (p.err) p.err[116] = S.canary;
     }
-    const IqTab itab = make_tab(tab, lane);
+    const IqTab itab = make_tab(smem + M.tab, lane);
     const AbsTab atab = make_abs_tab(lane);
-    uint32_t seq = 0;               // the ring sequence number of the next unit, identical in every consumer
-    int claim_base = 0;
-    unsigned target = 0;
     const int T = p.T, H = p.H, F = p.F, E = p.E, K = p.K;
     const XqView xv{xq_codes, xq_d, H};
     const XqView hsv{hs_codes, hs_d, p.FS};
     const XqView hqv{hq_codes, hq_d, F};
-
-    auto claim = [&](int n, int& k) -> bool {   // this warp's next unit of the phase, or false
-        int v = 0;
-        if (lane == 0) v = atomicAdd(&S.claim, 1);
-        v = __shfl_sync(0xffffffffu, v, 0);
-        k = v - claim_base;
-        return k < n;
-    };
-    int cur_layer = 0, cur_phase = 0;
-    auto wait_full = [&](uint32_t s) -> bool {
-        const uint32_t slot = s % kSlots, par = (s / kSlots) & 1u;
-        if (lane == 0) {
-            S.warp_unit[warp] = (int) s;
-            S.warp_state[warp] = 1;
-        }
-        const uint64_t t0 = globaltimer();
-        bool failed = false;
-        while (S.slot_lap[slot] < (int) (s / kSlots)) {   // the producer has not started this lap on the slot yet
-            if (globaltimer() - t0 > kWaitNs) {
-                failed = true;
-                break;
-            }
-        }
-        bool done = failed || mbar_try_wait(&S.full[slot], par);
-        while (!done) {   // every lane observes the phase itself (the bulk copy's bytes are then visible to it)
-            done = mbar_try_wait(&S.full[slot], par);
-            if (!done && globaltimer() - t0 > kWaitNs) {
-                failed = true;
-                break;
-            }
-        }
-        if (__all_sync(0xffffffffu, !failed)) {   // one verdict for the whole warp
-            if (lane == 0) S.warp_state[warp] = 2;
-            return true;
-        }
-        {
-            {
-                report_error(p.err, 0x330u | ((unsigned) cur_phase << 12));
-                if (p.err && atomicCAS(p.err + 61, 0u, 1u) == 0u) {
-                    p.err[1] = s | ((unsigned) cur_layer << 24);
-                    p.err[2] = (unsigned) S.prod_seq;
-                    p.err[3] = (unsigned) S.prod_state;
-                    p.err[4] = (unsigned) claim_base | (blockIdx.x << 20);
-                    p.err[5] = (unsigned) S.claim;
-                    for (int w = 0; w < kDecConsumers; ++w)
-                        p.err[6 + w] = (unsigned) S.warp_unit[w] | ((unsigned) S.warp_state[w] << 16);
-                    for (int q = 0; q < kSlots; ++q) {   // raw mbarrier words of every slot
-                        const unsigned long long f = *(volatile unsigned long long*) &S.full[q];
-                        const unsigned long long e = *(volatile unsigned long long*) &S.empty[q];
-                        p.err[24 + 4 * q] = (unsigned) f;
-                        p.err[25 + 4 * q] = (unsigned) (f >> 32);
-                        p.err[26 + 4 * q] = (unsigned) e;
-                        p.err[27 + 4 * q] = (unsigned) (e >> 32);
-                    }
-                    __threadfence();
-                }
-                S.abort = 1;
-                return false;
-            }
-        }
-        return true;
-    };
-    auto release = [&](uint32_t s) {
-        __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(&S.empty[s % kSlots]);
-            S.warp_state[warp] = 3;
-        }
-    };
-    auto end_phase = [&](int n) {   // every consumer warp overshoots its claims once
-        claim_base += n + kDecConsumers;
-        seq += (uint32_t) n;
-    };
-
     const int Cs = H / 32 * 4;           // Q8_0 calls per shared gate/up row
     const int Csd = p.FS / 32 * 4;       // Q8_0 calls per shared down row
 
+    WarpStream st;
+    st.nslot = p.nslot;
+    st.bar = S.bar[warp];
+    st.slot[0] = p.smem_base + slot_offset(M, p.nslot, warp, 0);
+    st.slot[1] = p.smem_base + slot_offset(M, p.nslot, warp, 1);
+    auto fail = [&](unsigned site, int l) {   // a wait gave up
+        report_detail(p.err, site, (unsigned) warp | ((unsigned) l << 8), st.issued, st.consumed, blockIdx.x);
+        S.abort = 1;
+    };
+
+    // P1 units: the same CTA range every layer; this warp's are r1.lo + warp + j kDecWarps
+    const Range r1 = split(p1_units(p), gridDim.x, blockIdx.x);
+    const int n1w = per_warp(r1.hi - r1.lo, warp);
+    int pre1 = 0;   // P1 units of the coming layer already issued
+    {
+        const DecLayer L0 = p.layers[0];
+        while (pre1 < n1w && st.can_issue()) {
+            BulkCopy c[2];
+            const int n = p1_copies(p, L0, r1.lo + warp + pre1 * kDecWarps, c);
+            st.issue(c, n, lane);
+            ++pre1;
+        }
+    }
+
     for (int l = 0; l < p.n_layers; ++l) {
         if (threadIdx.x == 0) stamp(p, l, 0);
+        const DecLayer L = p.layers[l];
+        const uint32_t tag = (uint32_t) l + 1u;   // what this layer writes
         // ---------------------------------------------------------------- P0: rms and q8_1 of every token
         // The reference's order (k_moe_out_small): 256 slots s = sum over i = s mod 256 of x_i^2 in order, then the
         // halving tree; thread i < 32 forms the tree's 32-slot level from 8 slots, shuffles finish it.
         float* xs = parts;   // the token's row in shared memory (the parts buffer is free until P3)
+        const Range own = my_chunks(p);
+        const int nown = (own.hi - own.lo) * p.R, own0 = own.lo * p.R;
         for (int t = 0; t < T; ++t) {
-            const float* xr = p.x + (size_t) t * H;
-            for (int i = threadIdx.x; i < H / 4; i += kDecCThreads) ((float4*) xs)[i] = __ldcg((const float4*) xr + i);
+            if (l == 0) {   // the caller's x
+                const float* xr = p.x + (size_t) t * H;
+                for (int i = threadIdx.x; i < H / 4; i += kDecCThreads) ((float4*) xs)[i] = __ldcg((const float4*) xr + i);
+            } else {        // every CTA's rows of the previous layer
+                poll_copy(p, S, p.xt + (size_t) t * H, H, tag - 1u, xs, threadIdx.x, kDecCThreads, 0x340u);
+            }
             named_sync(1, kDecCThreads);
+            if (threadIdx.x < nown) S.xown[t][threadIdx.x] = xs[own0 + threadIdx.x];
             if (threadIdx.x < 256) {
                 float s = 0.0f;
                 for (int i = threadIdx.x; i < H; i += 256) s += xs[i] * xs[i];
@@ -645,27 +611,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
             quantize_blocks<true>(xs, H, xq_codes + (size_t) t * H, xq_d + t * (H / 32), warp, lane, kDecConsumers);
             if (t + 1 < T) named_sync(1, kDecCThreads);
         }
-        named_sync(1, kDecCThreads);
+        if (named_sync_or(1, kDecCThreads, S.abort)) break;
         if (threadIdx.x == 0) stamp(p, l, 1);
-        cur_layer = l;
-        cur_phase = 1;
 
         // ---------------------------------------------------------------- P1: router rows, shared gate/up
         {
-            const int n1 = p1_units(p);
-            const Range r1 = split(n1, gridDim.x, blockIdx.x);
-            const int mine = r1.hi - r1.lo;
-            int k;
-            while (claim(mine, k)) {
-                const uint32_t s = seq + (uint32_t) k;
-                if (!wait_full(s)) break;
-                const uint8_t* buf = ring + (size_t) (s % kSlots) * kSlotBytes;
-                const int u = r1.lo + k;
+            const float* xs = parts;   // h of the token (T = 1), left by P0
+            int next1 = pre1;
+            for (int j = 0; j < n1w; ++j) {
+                const uint8_t* buf = st.wait(smem, p.smem_base);
+                if (!buf) {
+                    fail(0x331u, l);
+                    break;
+                }
+                const int u = r1.lo + warp + j * kDecWarps;
                 if (u < 2 * (E + 1)) {
                     const int o = u >> 1, half = u & 1;
                     const float4* wr = (const float4*) buf;
                     for (int t = 0; t < T; ++t) {
                         const float* xr = p.x + (size_t) t * H + half * (H / 2);
+                        const uint64_t* xw = p.xt + (size_t) t * H + half * (H / 2);
                         const float r = S.rms[t];
                         float acc = 0.0f;
                         if (T == 1) {   // h of the only token is in shared memory
@@ -679,13 +644,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
 #pragma unroll 4
                             for (int i = lane; i < H / 8; i += 32) {
                                 const float4 w = wr[i];
-                                const float4 xv4 = __ldcg((const float4*) xr + i);
+                                float4 xv4;
+                                if (l == 0) {
+                                    xv4 = __ldcg((const float4*) xr + i);
+                                } else {   // the words P0 polled: their tags are this layer's input already
+                                    uint64_t a, b, c, d;
+                                    ld_tag2(xw + 4 * i, a, b);
+                                    ld_tag2(xw + 4 * i + 2, c, d);
+                                    xv4 = make_float4(tag_val(a), tag_val(b), tag_val(c), tag_val(d));
+                                }
                                 acc += w.x * __fmul_rn(xv4.x, r) + w.y * __fmul_rn(xv4.y, r) + w.z * __fmul_rn(xv4.z, r) +
                                        w.w * __fmul_rn(xv4.w, r);
                             }
                         }
                         acc = warp_sum(acc);
-                        if (lane == 0) p.logits[((size_t) t * (E + 1) + o) * 2 + half] = acc;
+                        if (lane == 0) st_tag(p.logits + ((size_t) t * (E + 1) + o) * 2 + half, acc, tag);
                     }
                 } else {
                     const int r = u - 2 * (E + 1);
@@ -703,85 +676,101 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         }
                         sg = warp_sum(sg);
                         su = warp_sum(su);
-                        if (lane == 0) p.hsh[(size_t) t * p.FS + r] = act_value(ACT_SWIGLU, sg, su, INFINITY);
+                        if (lane == 0) st_tag(p.hsh + (size_t) t * p.FS + r, act_value(ACT_SWIGLU, sg, su, INFINITY), tag);
                     }
                 }
-                release(s);
+                st.release();
+                if (next1 < n1w) {
+                    BulkCopy c[2];
+                    const int n = p1_copies(p, L, r1.lo + warp + next1 * kDecWarps, c);
+                    st.issue(c, n, lane);
+                    ++next1;
+                }
             }
-            end_phase(mine);
         }
         if (threadIdx.x == 0) stamp(p, l, 2);
-        if (!grid_barrier(p, S, target, 0x340u)) break;
-        if (threadIdx.x == 0) stamp(p, l, 3);
 
         // ---------------------------------------------------------------- R: routing, grouping; shared hidden -> q8_1
-        for (int t = warp; t < T; t += kDecConsumers) {
-            const float* lg = p.logits + (size_t) t * (E + 1) * 2;
-            float values[V];
+        // Warps [0, gw) route (once every CTA's logits of the token are in) and group while the others wait at the
+        // barrier: no other warp of the CTA polls global memory meanwhile (polling loads queue ahead of the routing
+        // warps' local-memory accesses).
+        const int gw = T <= 4 ? 4 : kDecConsumers;
+        if (warp < gw) {
+            for (int t = warp; t < T; t += gw) {
+                const uint64_t* lg = p.logits + (size_t) t * (E + 1) * 2;
+                float values[V];
+                float gate_logit = 0.0f;
+                const uint64_t t0 = globaltimer();
+                for (;;) {
+                    bool ok = true;
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-                const float2 pp = __ldcg((const float2*) lg + lane + i * 32);
-                values[i] = pp.x + pp.y;
-            }
-            float maximum = -INFINITY;
+                    for (int i = 0; i < V; ++i) {
+                        uint64_t a, b;
+                        ld_tag2(lg + 2 * (lane + i * 32), a, b);
+                        values[i] = tag_val(a) + tag_val(b);
+                        ok &= tag_is(a, tag) & tag_is(b, tag);
+                    }
+                    if (lane == 0) {
+                        uint64_t a, b;
+                        ld_tag2(lg + 2 * E, a, b);
+                        gate_logit = tag_val(a) + tag_val(b);
+                        ok &= tag_is(a, tag) & tag_is(b, tag);
+                    }
+                    if (ok || poll_give_up(p, S, t0, 0x345u)) break;
+                }
+                if (threadIdx.x == 0) stamp(p, l, 9);
+                float maximum = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < V; ++i) maximum = fmaxf(maximum, values[i]);
-            maximum = warp_max(maximum);
-            float sum = 0.0f;
+                for (int i = 0; i < V; ++i) maximum = fmaxf(maximum, values[i]);
+                maximum = warp_max(maximum);
+                float sum = 0.0f;
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-                values[i] = fexp_fm(values[i] - maximum);
-                sum += values[i];
-            }
-            const float reciprocal = frcp_fm(warp_sum(sum));
+                for (int i = 0; i < V; ++i) {
+                    values[i] = fexp_fm(values[i] - maximum);
+                    sum += values[i];
+                }
+                const float reciprocal = frcp_fm(warp_sum(sum));
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
-                values[i] *= reciprocal;
-                if (__isnanf(values[i])) values[i] = -FLT_MAX;
-            }
-            float selected = 0.0f, selected_sum = 0.0f;
-            for (int rank = 0; rank < K; ++rank) {
-                float best = values[0];
-                int expert = lane;
+                for (int i = 0; i < V; ++i) {
+                    values[i] *= reciprocal;
+                    if (__isnanf(values[i])) values[i] = -FLT_MAX;
+                }
+                float selected = 0.0f, selected_sum = 0.0f;
+                uint32_t taken = 0;   // this lane's values already picked (they count as -inf, as in the reference)
+                for (int rank = 0; rank < K; ++rank) {
+                    float best = (taken & 1u) ? -INFINITY : values[0];
+                    int expert = lane;
 #pragma unroll
-                for (int i = 1; i < V; ++i)
-                    if (values[i] > best) {
-                        best = values[i];
-                        expert = lane + i * 32;
+                    for (int i = 1; i < V; ++i) {
+                        const float v = (taken >> i & 1u) ? -INFINITY : values[i];
+                        if (v > best) {
+                            best = v;
+                            expert = lane + i * 32;
+                        }
                     }
 #pragma unroll
-                for (int m = 16; m; m >>= 1) {
-                    const float ob = __shfl_xor_sync(0xffffffffu, best, m);
-                    const int oi = __shfl_xor_sync(0xffffffffu, expert, m);
-                    if (ob > best || (ob == best && oi < expert)) {
-                        best = ob;
-                        expert = oi;
+                    for (int m = 16; m; m >>= 1) {
+                        const float ob = __shfl_xor_sync(0xffffffffu, best, m);
+                        const int oi = __shfl_xor_sync(0xffffffffu, expert, m);
+                        if (ob > best || (ob == best && oi < expert)) {
+                            best = ob;
+                            expert = oi;
+                        }
                     }
+                    if ((expert & 31) == lane) {
+                        taken |= 1u << (expert / 32);
+                        S.ids[t * K + rank] = expert;
+                        selected_sum += best;
+                    }
+                    if (rank == lane) selected = best;
                 }
-                if ((expert & 31) == lane) {
-#pragma unroll
-                    for (int i = 0; i < V; ++i)
-                        if (i == expert / 32) values[i] = -INFINITY;
-                    S.ids[t * K + rank] = expert;
-                    selected_sum += best;
-                }
-                if (rank == lane) selected = best;
+                selected_sum = fmaxf(warp_sum(selected_sum), 6.103515625e-5f);
+                const float inv = frcp_fm(selected_sum);
+                if (lane < K) S.w[t * K + lane] = selected * inv;
+                if (lane == 0) S.gs[t] = frcp_fm(1.0f + fexp_fm(-gate_logit));
             }
-            selected_sum = fmaxf(warp_sum(selected_sum), 6.103515625e-5f);
-            const float inv = frcp_fm(selected_sum);
-            if (lane < K) S.w[t * K + lane] = selected * inv;
-            if (lane == 0) {
-                const float2 pg = __ldcg((const float2*) lg + E);
-                S.gs[t] = frcp_fm(1.0f + fexp_fm(-(pg.x + pg.y)));
-            }
-        }
-        // the shared expert's hidden vectors into q8_1, by the warps that route no token
-        if (T < kDecConsumers && warp >= T)
-            quantize_blocks<false>(p.hsh, T * p.FS, hs_codes, hs_d, warp - T, lane, kDecConsumers - T);
-        else if (T >= kDecConsumers)
-            quantize_blocks<false>(p.hsh, T * p.FS, hs_codes, hs_d, warp, lane, kDecConsumers);
-        named_sync(1, kDecCThreads);
-        {
+            if (threadIdx.x == 0) stamp(p, l, 10);
+            named_sync(2, gw * 32);
             const int n_ent = T * K;
             const int e = threadIdx.x;
             int id = 0, rank = 0;
@@ -798,7 +787,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     p.w_rec[(size_t) l * n_ent + e] = S.w[e];
                 }
             }
-            named_sync(1, kDecCThreads);
+            named_sync(2, gw * 32);
             if (e < n_ent) {   // group g starts at the sorted position of the first entry of its expert
                 const int pos = rank;
                 const int prev_id = pos > 0 ? S.ids[S.ent_dst[pos - 1]] : -1;
@@ -815,83 +804,106 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 S.grp_start[G] = n_ent;
                 S.n_groups = G;
             }
-            named_sync(1, kDecCThreads);
-            if (threadIdx.x == 0) mbar_arrive(&S.route);   // the producer may stream this layer's P2 and P3
+            named_sync(2, gw * 32);
+            if (threadIdx.x == 0) stamp(p, l, 3);
         }
+        if (named_sync_or(1, kDecCThreads, S.abort)) break;
         const int ng = S.n_groups;
+
+        // This warp's units after the routing, in stream order: its P2 units, its P3 units, the next layer's P1 units.
+        const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
+        const Range r2 = split(n2, gridDim.x, blockIdx.x);
+        const int n2w = per_warp(r2.hi - r2.lo, warp);
+        const Range ch = my_chunks(p);
+        const int nch = ch.hi - ch.lo, ntask = nch * ng;
+        const int n3w = per_warp(p3_units(p, ng), warp);
+        const bool more = l + 1 < p.n_layers;
+        const DecLayer Ln = more ? p.layers[l + 1] : L;
+        const int npost = n2w + n3w + (more ? n1w : 0);
+        int post = 0;
+        auto issue_post = [&]() {
+            BulkCopy c[2];
+            int n;
+            if (post < n2w)
+                n = p2_copies(p, L, S, ng, r2.lo + warp + post * kDecWarps, c);
+            else if (post < n2w + n3w)
+                n = p3_copies(p, L, S, ng, ch, warp + (post - n2w) * kDecWarps, c);
+            else
+                n = p1_copies(p, Ln, r1.lo + warp + (post - n2w - n3w) * kDecWarps, c);
+            st.issue(c, n, lane);
+            ++post;
+        };
+        while (post < npost && st.can_issue()) issue_post();
+        // the shared hidden vector into q8_1 (every CTA's P1) while this warp's first P2 rows land
+        quantize_tagged(p, S, p.hsh, T * p.FS, tag, hs_codes, hs_d, warp, lane, kDecConsumers, 0x348u);
+        if (named_sync_or(1, kDecCThreads, S.abort)) break;
         if (threadIdx.x == 0) stamp(p, l, 4);
 
         // ---------------------------------------------------------------- P2: routed gate/up, shared down
-        cur_phase = 2;
-        {
-            const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
-            const Range r2 = split(n2, gridDim.x, blockIdx.x);
-            const int mine = r2.hi - r2.lo;
-            int k;
-            while (claim(mine, k)) {
-                const uint32_t s = seq + (uint32_t) k;
-                if (!wait_full(s)) break;
-                const uint8_t* buf = ring + (size_t) (s % kSlots) * kSlotBytes;
-                const int u = r2.lo + k;
-                if (u < nrt) {
-                    const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * F);
-                    for (int i = i0; i < i1; ++i) {   // the unit's gate rows, then its up rows
-                        const int g = i / F, r = i % F;
-                        const uint8_t* gate = buf + (size_t) (i - i0) * p.gu_row;
-                        const uint8_t* up = gate + (size_t) (i1 - i0) * p.gu_row;
-                        const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
-                        for (int eb = e0; eb < e1; ++eb) {   // decode groups rarely hold more than one entry
-                            const int tok = S.ent_tok[eb];
-                            auto src = [&](int blk) { return xv.block(tok, blk); };
-                            Fmt<T_IQ3_XXS>::Act a[2];
+        for (int j = 0; j < n2w; ++j) {
+            const uint8_t* buf = st.wait(smem, p.smem_base);
+            if (!buf) {
+                fail(0x332u, l);
+                break;
+            }
+            const int u = r2.lo + warp + j * kDecWarps;
+            if (u < nrt) {
+                const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * F);
+                for (int i = i0; i < i1; ++i) {   // the unit's gate rows, then its up rows
+                    const int g = i / F, r = i % F;
+                    const uint8_t* gate = buf + (size_t) (i - i0) * p.gu_row;
+                    const uint8_t* up = gate + (size_t) (i1 - i0) * p.gu_row;
+                    const int e0 = S.grp_start[g], e1 = S.grp_start[g + 1];
+                    for (int eb = e0; eb < e1; ++eb) {   // decode groups rarely hold more than one entry
+                        const int tok = S.ent_tok[eb];
+                        auto src = [&](int blk) { return xv.block(tok, blk); };
+                        Fmt<T_IQ3_XXS>::Act a[2];
 #pragma unroll
-                            for (int j = 0; j < 2; ++j) a[j] = Fmt<T_IQ3_XXS>::act(src, iq3_par_call(lane, j));
-                            const float sg = iq3_row_par(gate, lane, a, atab);
-                            const float su = iq3_row_par(up, lane, a, atab);
-                            if (lane == 16) p.hbuf[(size_t) S.ent_dst[eb] * F + r] = act_value(ACT_SWIGLU, sg, su, INFINITY);
-                        }
-                    }
-                } else {
-                    const int r0 = (u - nrt) * p.sd_per_unit;
-                    for (int t0 = 0; t0 < T; t0 += 2) {
-                        const int nc = min(2, T - t0);
-                        typename Fmt<T_Q8_0>::Act a[2][2];
-#pragma unroll
-                        for (int c = 0; c < 2; ++c) {
-                            if (c >= nc) break;
-                            auto src = [&](int blk) { return hsv.block(t0 + c, blk); };
-#pragma unroll
-                            for (int j = 0; j < 2; ++j)
-                                if (lane + 32 * j < Csd) a[c][j] = Fmt<T_Q8_0>::act(src, lane + 32 * j);
-                        }
-                        for (int rr = 0; rr < p.sd_per_unit; ++rr) {
-                            float sv[2];
-                            row_dot<T_Q8_0, 2, 2>(buf + (size_t) rr * p.sd_row, Csd, lane, a, nc, itab, sv);
-                            if (lane < nc) p.sh_out[(size_t) (t0 + lane) * H + r0 + rr] = lane == 0 ? sv[0] : sv[1];
-                        }
+                        for (int j = 0; j < 2; ++j) a[j] = Fmt<T_IQ3_XXS>::act(src, iq3_par_call(lane, j));
+                        const float sg = iq3_row_par(gate, lane, a, atab);
+                        const float su = iq3_row_par(up, lane, a, atab);
+                        if (lane == 16)
+                            st_tag(p.hbuf + (size_t) S.ent_dst[eb] * F + r, act_value(ACT_SWIGLU, sg, su, INFINITY), tag);
                     }
                 }
-                release(s);
+            } else {
+                const int r0 = (u - nrt) * p.sd_per_unit;
+                for (int t0 = 0; t0 < T; t0 += 2) {
+                    const int nc = min(2, T - t0);
+                    typename Fmt<T_Q8_0>::Act a[2][2];
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        if (c >= nc) break;
+                        auto src = [&](int blk) { return hsv.block(t0 + c, blk); };
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+                            if (lane + 32 * j < Csd) a[c][j] = Fmt<T_Q8_0>::act(src, lane + 32 * j);
+                    }
+                    for (int rr = 0; rr < p.sd_per_unit; ++rr) {
+                        float sv[2];
+                        row_dot<T_Q8_0, 2, 2>(buf + (size_t) rr * p.sd_row, Csd, lane, a, nc, itab, sv);
+                        if (lane < nc) st_tag(p.sh_out + (size_t) (t0 + lane) * H + r0 + rr, lane == 0 ? sv[0] : sv[1], tag);
+                    }
+                }
             }
-            end_phase(mine);
+            st.release();
+            if (post < npost) issue_post();
         }
         if (threadIdx.x == 0) stamp(p, l, 5);
-        if (!grid_barrier(p, S, target, 0x350u)) break;
-        if (threadIdx.x == 0) stamp(p, l, 6);
 
         // ---------------------------------------------------------------- P3: routed down rows, combine
-        cur_phase = 3;
         {
-            quantize_blocks<false>(p.hbuf, T * K * F, hq_codes, hq_d, warp, lane, kDecConsumers);
-            named_sync(1, kDecCThreads);
-            const Range ch = my_chunks(p);
-            const int nch = ch.hi - ch.lo, ntask = nch * ng;
-            const int mine = p3_units(p, ng);
-            int k;
-            while (claim(mine, k)) {
-                const uint32_t s = seq + (uint32_t) k;
-                if (!wait_full(s)) break;
-                const uint8_t* buf = ring + (size_t) (s % kSlots) * kSlotBytes;
+            named_sync(1, kDecCThreads);   // P2's activations (the union P3's codes overwrite) are no longer read
+            quantize_tagged(p, S, p.hbuf, T * K * F, tag, hq_codes, hq_d, warp, lane, kDecConsumers, 0x350u);
+            if (named_sync_or(1, kDecCThreads, S.abort)) break;
+            if (threadIdx.x == 0) stamp(p, l, 6);
+            for (int j = 0; j < n3w; ++j) {
+                const uint8_t* buf = st.wait(smem, p.smem_base);
+                if (!buf) {
+                    fail(0x333u, l);
+                    break;
+                }
+                const int k = warp + j * kDecWarps;
                 const int i0 = k * p.dn_per_unit, i1 = min(i0 + p.dn_per_unit, ntask);
                 for (int i = i0; i < i1; ++i) {
                     const int cl = i % nch, g = i / nch;   // chunk index within this CTA, group (group-major tasks)
@@ -915,9 +927,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         if ((lane & 7) == 0) parts[ent * kDecMaxRows + cl * p.R + (lane >> 3)] = v;
                     }
                 }
-                release(s);
+                st.release();
+                if (post < npost) issue_post();
             }
-            end_phase(mine);
             named_sync(1, kDecCThreads);
             // combine this CTA's rows for every token
             const int nrows = (ch.hi - ch.lo) * p.R;
@@ -927,13 +939,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 const float* wr = S.w + t * K;
                 float acc = wr[0] * parts[(t * K) * kDecMaxRows + lr];
                 for (int kk = 1; kk < K; ++kk) acc = fmaf(wr[kk], parts[(t * K + kk) * kDecMaxRows + lr], acc);
-                acc += S.gs[t] * __ldcg(p.sh_out + (size_t) t * H + row);
-                p.x[(size_t) t * H + row] = __ldcg(p.x + (size_t) t * H + row) + acc;
+                const uint64_t* so = p.sh_out + (size_t) t * H + row;
+                uint64_t w = ld_tag(so);
+                const uint64_t t0 = globaltimer();
+                while (!tag_is(w, tag) && !poll_give_up(p, S, t0, 0x360u)) w = ld_tag(so);
+                acc += S.gs[t] * tag_val(w);
+                const float xn = S.xown[t][lr] + acc;
+                p.x[(size_t) t * H + row] = xn;
+                st_tag(p.xt + (size_t) t * H + row, xn, tag);
             }
         }
+        pre1 = post > n2w + n3w ? post - n2w - n3w : 0;
         if (threadIdx.x == 0) stamp(p, l, 7);
-        if (!grid_barrier(p, S, target, 0x360u)) break;
+        if (named_sync_or(1, kDecCThreads, S.abort)) break;   // (the next layer's P0 reuses the parts buffer)
         if (threadIdx.x == 0) stamp(p, l, 8);
+    }
+    // wind down: every copy this warp issued has landed before the CTA may exit (bounded)
+    while (st.consumed < st.issued) {
+        if (!st.wait(smem, p.smem_base)) break;
+        st.release();
     }
 }
 

@@ -128,6 +128,36 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// 16 bytes global -> shared through L2 (cp.async.cg: the load/store unit, not the bulk-copy engine, so a warp issues 32
+// of them per instruction), and an arrive on an mbarrier once every cp.async this thread issued before has landed
+// (.noinc: the barrier's expected count includes the arriving threads).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Tagged exchange words between the CTAs of one launch: a float and the tag of the step that wrote it in one 8-byte
+// word (low half the value bits, high half the tag), stored and loaded as single 64-bit accesses at gpu scope.  A
+// reader polls the words it needs until every tag is the one it expects: the data is its own completion flag, one
+// L2 round trip once the writer has stored it and no grid-wide barrier.
+__device__ __forceinline__ void st_tag(uint64_t* p, float v, uint32_t tag) {
+    const uint64_t w = (uint64_t) __float_as_uint(v) | ((uint64_t) tag << 32);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tag(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// Two consecutive words (16-byte aligned): two 64-bit accesses, each single-copy atomic.
+__device__ __forceinline__ void ld_tag2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ float tag_val(uint64_t w) { return __uint_as_float((uint32_t) w); }
+__device__ __forceinline__ bool tag_is(uint64_t w, uint32_t tag) { return (uint32_t) (w >> 32) == tag; }
+
 // Non-blocking probe of a phase (test_wait returns at once; try_wait may suspend the thread for a while).
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
