@@ -205,7 +205,10 @@ __device__ bool poll_copy(const DecParams& p, DecShared& S, const uint64_t* src,
 struct Range {
     int lo, hi;
 };
-__device__ __forceinline__ Range split(int n, int parts, int i) { return {(int) ((long long) n * i / parts), (int) ((long long) n * (i + 1) / parts)}; }
+// 32-bit products (n * parts < 2^32 for every split here: at most 2^16 units over the SMs).
+__device__ __forceinline__ Range split(int n, int parts, int i) {
+    return {(int) ((uint32_t) n * (uint32_t) i / (uint32_t) parts), (int) ((uint32_t) n * (uint32_t) (i + 1) / (uint32_t) parts)};
+}
 
 __device__ __forceinline__ int p1_units(const DecParams& p) { return 2 * (p.E + 1) + p.FS; }
 __device__ __forceinline__ int p2_rt_units(const DecParams& p, int ng) { return (ng * p.F + p.rt_per_unit - 1) / p.rt_per_unit; }
@@ -691,9 +694,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         if (threadIdx.x == 0) stamp(p, l, 2);
 
         // ---------------------------------------------------------------- R: routing, grouping; shared hidden -> q8_1
-        // Warps [0, gw) route (once every CTA's logits of the token are in) and group while the others wait at the
-        // barrier: no other warp of the CTA polls global memory meanwhile (polling loads queue ahead of the routing
-        // warps' local-memory accesses).
+        // Warps [0, gw) route (once every CTA's logits of the token are in) and group while the other warps wait.
         const int gw = T <= 4 ? 4 : kDecConsumers;
         if (warp < gw) {
             for (int t = warp; t < T; t += gw) {
@@ -735,28 +736,30 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     values[i] *= reciprocal;
                     if (__isnanf(values[i])) values[i] = -FLT_MAX;
                 }
+                // Top-k as the reference's argmax rounds (largest value, then lowest expert id), on order-preserving
+                // integer keys: a lane's best key, one warp max reduction, then one min reduction over the ids that hold it.
+                uint32_t key[V];
+#pragma unroll
+                for (int i = 0; i < V; ++i) {
+                    const uint32_t b = __float_as_uint(values[i]);
+                    key[i] = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+                }
                 float selected = 0.0f, selected_sum = 0.0f;
-                uint32_t taken = 0;   // this lane's values already picked (they count as -inf, as in the reference)
+                uint32_t taken = 0;   // this lane's keys already picked: 0, below every value (the reference's -inf)
                 for (int rank = 0; rank < K; ++rank) {
-                    float best = (taken & 1u) ? -INFINITY : values[0];
-                    int expert = lane;
+                    uint32_t kb = (taken & 1u) ? 0u : key[0];
+                    int ib = 0;
 #pragma unroll
                     for (int i = 1; i < V; ++i) {
-                        const float v = (taken >> i & 1u) ? -INFINITY : values[i];
-                        if (v > best) {
-                            best = v;
-                            expert = lane + i * 32;
+                        const uint32_t ki = (taken >> i & 1u) ? 0u : key[i];
+                        if (ki > kb) {
+                            kb = ki;
+                            ib = i;
                         }
                     }
-#pragma unroll
-                    for (int m = 16; m; m >>= 1) {
-                        const float ob = __shfl_xor_sync(0xffffffffu, best, m);
-                        const int oi = __shfl_xor_sync(0xffffffffu, expert, m);
-                        if (ob > best || (ob == best && oi < expert)) {
-                            best = ob;
-                            expert = oi;
-                        }
-                    }
+                    const uint32_t kmax = __reduce_max_sync(0xffffffffu, kb);
+                    const int expert = (int) __reduce_min_sync(0xffffffffu, kb == kmax ? (uint32_t) (lane + 32 * ib) : 0xffffffffu);
+                    const float best = __uint_as_float((kmax & 0x80000000u) ? (kmax & 0x7fffffffu) : ~kmax);
                     if ((expert & 31) == lane) {
                         taken |= 1u << (expert / 32);
                         S.ids[t * K + rank] = expert;
