@@ -26,9 +26,9 @@ sys.path.insert(0, ROOT)
 
 N_LAYERS = 40   # --layers changes it for profiling captures only (a smaller device footprint); the bench is 40
 # DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch
-# (profiles/k_decode_layers_qwen_decode_T1_4layers_full.md: 64.19 MB per launch); traffic grows with the layer count,
+# (profiles/k_decode_layers_qwen_decode_T1_4layers_full.md: 61.77 MB per launch); traffic grows with the layer count,
 # so a launch of N layers moves N times this.
-TRAFFIC_PER_LAYER_T1 = 64.19e6 / 4
+TRAFFIC_PER_LAYER_T1 = 61.77e6 / 4
 METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
 
 
