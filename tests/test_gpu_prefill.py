@@ -48,9 +48,15 @@ def _routed_case(cfg, T_tok, K, E_mat, seed):
     return layer, x, ids
 
 
-@pytest.mark.parametrize("T_tok,K", [(200, 2), (37, 8)])
-def test_prefill_routed_gemma_vs_oracle(cuda, T_tok, K):
-    cfg = synth.GEMMA
+# weight formats: Q4_0 (Gemma, C2), Q4_K gate/up + Q6_K down (LFM2, C3), IQ3_XXS (Qwen, C1 weights),
+# IQ3_XXS gate/up + IQ3_S down (Qwen expert-parallel, C4)
+CASES = [("gemma", 200, 2), ("gemma", 37, 8), ("lfm", 150, 4), ("qwen", 120, 8), ("qwen_ep", 96, 8)]
+CFGS = {"gemma": synth.GEMMA, "lfm": synth.LFM, "qwen": synth.QWEN, "qwen_ep": synth.QWEN_EP}
+
+
+@pytest.mark.parametrize("name,T_tok,K", CASES)
+def test_prefill_routed_vs_oracle(cuda, name, T_tok, K):
+    cfg = CFGS[name]
     H, F, E_mat = cfg["n_embd"], cfg["n_ff"], 8
     layer, x, ids = _routed_case(cfg, T_tok, K, E_mat, seed=21)
     L = T.native_expert_layout(cfg["gu_type"], cfg["d_type"], H, F)
@@ -105,8 +111,8 @@ def test_prefill_dense_shared_gemma_vs_oracle(cuda):
 
 
 def test_prefill_rejects_unsupported(cuda):
-    cfg = synth.QWEN   # IQ3_XXS weights have no prefill kernel yet
-    L = T.native_expert_layout(cfg["gu_type"], cfg["d_type"], cfg["n_embd"], cfg["n_ff"])
+    cfg = synth.QWEN   # Q8_0 routed weights: no prefill kernel (the reference's packs do not use them)
+    L = T.native_expert_layout(synth.T_Q8_0, synth.T_Q8_0, cfg["n_embd"], cfg["n_ff"])
     blobs = torch.zeros(int(L.bytes), dtype=torch.uint8, device="cuda")
     xq = torch.zeros((4, cfg["n_embd"] // 32 * 36), dtype=torch.uint8, device="cuda")
     with pytest.raises(T.TsbError, match="status -2"):

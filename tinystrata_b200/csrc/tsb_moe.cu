@@ -2,6 +2,7 @@
 // softmax / sigmoid top-k routers, decode grouping, grouped expert GEMVs, combine.  The C ABI is include/tsb_moe.h.
 #include "tsb_kernels.cuh"
 #include "tsb_prefill.cuh"
+#include "tsb_prefill_k.cuh"
 #include "../../include/tsb_moe.h"
 
 #include <cuda_runtime.h>
@@ -807,13 +808,38 @@ static int pf_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
     kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
     return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
 }
+template <int MODE, int WT, bool A16>
+static int pfx_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
+    auto kern = k_pf_gemm_x<MODE, WT, A16>;
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPxSmem) != cudaSuccess)
+            return cuda_status("prefill: shared memory");
+        attr = true;
+    }
+    kern<<<di->sms, kPfThreads, kPxSmem, s>>>(pp);
+    return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
+}
+template <int MODE, bool A16>
+static int pfx_launch_m(int wt, PfParams& pp, cudaStream_t s, DevInfo* di) {
+    switch (wt) {
+        case T_Q4_K: return pfx_launch_t<MODE, T_Q4_K, A16>(pp, s, di);
+        case T_Q6_K: return pfx_launch_t<MODE, T_Q6_K, A16>(pp, s, di);
+        case T_IQ3_XXS: return pfx_launch_t<MODE, T_IQ3_XXS, A16>(pp, s, di);
+        default: return pfx_launch_t<MODE, T_IQ3_S, A16>(pp, s, di);
+    }
+}
 extern "C" {
 // 16-byte windows where the rows allow them: activation rows of K / 32 q8_1 blocks (36 bytes), weight rows.
-static int pf_launch(int mode, PfParams& pp, cudaStream_t s) {
+static int pf_launch(int mode, int wt, PfParams& pp, cudaStream_t s) {
     DevInfo* di = dev_info();
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
     pp.err = di->err;
     const bool a16 = ((pp.K / 32) * 36) % 16 == 0 && (uintptr_t) pp.X % 16 == 0;
+    if (wt != T_Q4_0) {
+        if (mode == PF_GU) return a16 ? pfx_launch_m<PF_GU, true>(wt, pp, s, di) : pfx_launch_m<PF_GU, false>(wt, pp, s, di);
+        return a16 ? pfx_launch_m<PF_DOWN, true>(wt, pp, s, di) : pfx_launch_m<PF_DOWN, false>(wt, pp, s, di);
+    }
     const bool w16 = pp.w_row % 16 == 0 && (uintptr_t) pp.blobs % 16 == 0 && pp.blob_stride % 16 == 0 &&
                      pp.w_off % 16 == 0 && pp.up_off % 16 == 0;
     if (mode == PF_GU) {
@@ -829,10 +855,17 @@ static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob
     if (!L || !blobs || n_rows < 0 || n_groups < 1 || n_groups > kPfMaxGroups)
         return fail(TSB_ERR_ARG, "moe_prefill: arguments");
     const int t = mode == PF_GU ? L->gu_type : L->d_type;
-    if (t != T_Q4_0) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0 only)", t);
+    if (t != T_Q4_0 && t != T_Q4_K && t != T_Q6_K && t != T_IQ3_XXS && t != T_IQ3_S)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)", t);
     if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 128)
         return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd and n_ff multiples of 64, at least 128");
-    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || L->gu_row % 4 || L->d_row % 4)
+    const int64_t k = mode == PF_GU ? L->n_embd : L->n_ff;   // super-block formats: the contraction in 256-value blocks
+    if (t != T_Q4_0 && k % 256) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: K-quant / i-quant rows of 256-value blocks");
+    // Q4_0 rows are read in 4-byte words; the other formats' loaders take 2-byte aligned rows (Q6_K rows are 210 n / 256
+    // bytes), Q4_K's 16-byte ones (144-byte blocks)
+    const int64_t row = mode == PF_GU ? L->gu_row : L->d_row;
+    const int64_t ra = t == T_Q4_0 ? 4 : t == T_Q4_K ? 16 : 2;
+    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || row % ra)
         return fail(TSB_ERR_ALIGN, "moe_prefill: blob alignment");
     return TSB_OK;
 }
@@ -862,7 +895,7 @@ int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t b
     pp.Hq = (BlockQ8_1*) h_q8_1;
     pp.act = act;
     pp.limit = limit;
-    return pf_launch(PF_GU, pp, cs(stream));
+    return pf_launch(PF_GU, L->gu_type, pp, cs(stream));
 }
 
 int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
@@ -884,7 +917,7 @@ int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t
     pp.N = (int) L->n_embd;
     pp.X = (const BlockQ8_1*) h_q8_1;
     pp.D = out;
-    return pf_launch(PF_DOWN, pp, cs(stream));
+    return pf_launch(PF_DOWN, L->d_type, pp, cs(stream));
 }
 
 // ------------------------------------------------------------------------------------ no-allocation grouped experts
