@@ -146,6 +146,7 @@ def build_stack(cfg, T, device, seed=1):
 
 
 PREFILL_METRIC = "MoE-layer tokens/s (prefill, Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192)"
+PREFILL_LFM_METRIC = "MoE-layer tokens/s (prefill, LFM2.5-24B-A2B-shaped Q4_K/Q6_K layer, T=2048)"
 # int8 operations per layer of the C2 configuration: 2 T (K 3 H F + 3 H FS) + router 2 T H E (algorithmic, the
 # reference's MMQ work; the kernels here issue two fp16 tensor-core products per block, hi and lo weight parts)
 def prefill_ops(T, H, F, FS, K, E):
@@ -154,8 +155,9 @@ def prefill_ops(T, H, F, FS, K, E):
 
 def bench_prefill(args):
     """C2: one Gemma-4-26B-A4B-shaped layer (128 Q4_0 experts, top-8, dense Q4_0 shared FFN 2112, GELU-tanh) over
-    T = 8192 prompt tokens: router GEMM, routing, q8_1, dispatch, grouped gate/up + down on tcgen05, shared FFN,
-    combine, replayed as one CUDA graph."""
+    T = 8192 prompt tokens; C3 (--workload prefill_lfm): one LFM2.5-24B-A2B-shaped layer (64 experts, top-4 by sigmoid,
+    SwiGLU 1792, Q4_K gate/up, Q6_K down, no shared expert) over T = 2048 with router logits near N(0, 2): router GEMM,
+    routing, q8_1, dispatch, grouped gate/up + down on tcgen05, shared FFN, combine, replayed as one CUDA graph."""
     import torch
     import tinystrata_b200 as TS
     from tinystrata_b200 import synth
@@ -164,12 +166,16 @@ def bench_prefill(args):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    cfg = synth.GEMMA
+    lfm = args.workload == "prefill_lfm"
+    # C3's router logits N(0, 2): weights of sd 2 / sqrt(H) on RMS-normed inputs
+    cfg = dict(synth.LFM, router_sd=2.0 / np.sqrt(synth.LFM["n_embd"])) if lfm else synth.GEMMA
+    seed = 3 if lfm else 2
     T, H, F, FS, K, E = args.tokens, cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
-    st = synth.device_layers(cfg, 1, seed=2, device=device)
-    escale = torch.ones(E, dtype=torch.float32, device=device)
-    P = PrefillLayer(cfg, st["blobs"][0], st["routers"][0], st["sh_blobs"][0], max_tokens=T, escale=escale)
-    rng = np.random.default_rng(2)
+    st = synth.device_layers(cfg, 1, seed=seed, device=device)
+    escale = None if lfm else torch.ones(E, dtype=torch.float32, device=device)
+    P = PrefillLayer(cfg, st["blobs"][0], st["routers"][0], None if lfm else st["sh_blobs"][0], max_tokens=T,
+                     escale=escale)
+    rng = np.random.default_rng(seed)
     x0 = synth.rms_normed(rng, T, H)
     x0_dev = torch.from_numpy(x0).to(device)
     x0_host = torch.from_numpy(x0).pin_memory()
@@ -216,14 +222,20 @@ def bench_prefill(args):
     except (OSError, KeyError, ValueError):
         peak_kind = "fallback"
     achieved = ops / (ms * 1e-3) / 1e12
+    wbytes = int(st["blobs"][0].numel())
     line = {
-        "metric": PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "metric": PREFILL_LFM_METRIC if lfm else PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q8_1 x Q4_0 exact block dots on tcgen05 (fp16 operands: codes, weight hi + lo), fp32 block scaling",
+        "dtype": ("q8_1 x " + ("Q4_K / Q6_K" if lfm else "Q4_0") +
+                  " exact integer block dots on tcgen05 (fp16 operands holding integers), fp32 block scaling"),
         "data": "synthetic",
-        "config": {"workload": f"prefill T={T} through one Gemma-4-26B-A4B-shaped MoE layer", "tokens": T, "hidden": H,
-                   "experts": E, "top_k": K, "n_ff": F, "shared_n_ff": FS, "weights": "Q4_0",
-                   "l2": "inputs larger than L2 (428 MB of expert weights)"},
+        "config": {"workload": f"prefill T={T} through one " +
+                               ("LFM2.5-24B-A2B" if lfm else "Gemma-4-26B-A4B") + "-shaped MoE layer",
+                   "tokens": T, "hidden": H, "experts": E, "top_k": K, "n_ff": F, "shared_n_ff": FS,
+                   "weights": "Q4_K gate/up, Q6_K down" if lfm else "Q4_0",
+                   "l2": f"expert weights {wbytes / 1e6:.0f} MB (" +
+                         ("larger" if wbytes > 126e6 else "smaller") + " than L2); no flush between steps"},
         "us_per_layer": ms * 1e3,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s (int8-op/s, algorithmic)",
                      "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
@@ -238,6 +250,92 @@ def bench_prefill(args):
 
 
 EP_METRIC = "EP prefill MoE-layer tokens/s (Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192 per GPU, experts sharded)"
+EPQ_METRIC = "EP prefill MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped IQ3_XXS/IQ3_S layer, T=65536, experts sharded)"
+
+
+def bench_ep_qwen(args):
+    """C4: the Qwen3.6-35B-A3B-shaped layer (256 experts, IQ3_XXS gate/up, IQ3_S down, top-8 softmax, Q8_0 shared
+    expert gated by a sigmoid of the 257th router row) over T = 65536 prompt tokens split evenly over the ranks
+    (strong scaling), experts sharded 256 / N per GPU, router logits skewed by a Zipf(1.1) prior over the experts
+    (log p_e added to expert e's logit) so that the expert load is imbalanced.  Per step: router GEMM, routing, q8_1,
+    dispatch / return all-to-alls over NCCL, local experts and the shared expert on the tensor cores, gated sum.
+    Eager (host-synchronising counts), timed with CUDA events between barriers, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+    from tinystrata_b200.ep import ep_forward, gpu_expert_fn
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    else:
+        import tempfile
+        dist.init_process_group("nccl", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1,
+                                device_id=device)
+    cfg = synth.QWEN_EP
+    T_all = args.tokens if args.tokens > 1 else 65536
+    T = T_all // ws
+    H, F, FS, K, E = cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
+    per = E // ws
+    st = synth.device_layers(cfg, 1, seed=4, device=device)   # every rank draws the same layer, keeps its slice
+    blobs = st["blobs"][0][rank * per:(rank + 1) * per].contiguous()
+    router, sh = st["routers"][0], st["sh_blobs"][0]
+    del st
+    L = TS.native_expert_layout(cfg["gu_type"], cfg["d_type"], H, F)
+    Ls = TS.native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, FS)
+    zipf = torch.tensor(-1.1 * np.log(np.arange(1, E + 1)), dtype=torch.float32, device=device)
+    x0 = torch.from_numpy(synth.rms_normed(np.random.default_rng(4 + rank), T, H)).to(device)
+    fn = gpu_expert_fn(L, blobs, int(L.bytes), cfg["act"])
+
+    def step():
+        logits = TS.router_logits_f32(router, x0)                 # [T, E + 1]: the experts, then the shared gate
+        lg = logits[:, :E] + zipf
+        ids, w = TS.native_router_topk(lg.contiguous(), K)       # softmax top-8, renormalised (the Qwen router)
+        xq = TS.quantize_q8_1_rows(x0)
+        out = ep_forward(xq, ids, w, E, H, fn)
+        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xq, None, cfg["act"])
+        shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
+        return out.addcmul_(shared, torch.sigmoid(logits[:, E:E + 1]))
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    assert TS.device_error() == 0
+    if rank == 0:
+        ops = prefill_ops(T_all, H, F, FS, K, E + 1)
+        line = {
+            "metric": EPQ_METRIC, "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "q8_1 x IQ3_XXS / IQ3_S / Q8_0 exact integer block dots on tcgen05, fp32 block scaling",
+            "data": "synthetic (Zipf(1.1)-skewed router logits)",
+            "config": {"workload": f"expert-parallel prefill, {T_all} tokens over {ws} GPU(s), {per} of {E} "
+                                   "experts per GPU", "tokens": T_all, "tokens_per_gpu": T, "experts_per_gpu": per,
+                       "parallelism": f"ep{ws}",
+                       "collectives": "NCCL all_to_all_single (counts, q8_1 rows, picks; fp32 partial rows back)"},
+            "us_per_layer": ms * 1e3,
+            "roofline": {"bound": "tensor", "achieved": ops / (ms * 1e-3) / 1e12 / ws, "unit": "TFLOP/s per GPU",
+                         "note": "int8-op/s, algorithmic"},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
 
 
 def bench_ep(args):
@@ -329,14 +427,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "ep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen"],
                     help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192); "
-                         "ep: that layer expert-parallel over the launched ranks")
+                         "prefill_lfm: the C3 LFM2-shaped layer (--tokens 2048); ep: the C2 layer expert-parallel "
+                         "over the launched ranks; ep_qwen: the C4 Qwen IQ3 layer expert-parallel (65536 tokens)")
     args = ap.parse_args()
-    if args.workload in ("prefill", "ep"):
+    if args.workload == "ep_qwen":
+        return bench_ep_qwen(args)
+    if args.workload in ("prefill", "prefill_lfm", "ep"):
         if args.tokens == 1:
-            args.tokens = 8192
-        return bench_prefill(args) if args.workload == "prefill" else bench_ep(args)
+            args.tokens = 2048 if args.workload == "prefill_lfm" else 8192
+        return bench_prefill(args) if args.workload != "ep" else bench_ep(args)
     global N_LAYERS
     N_LAYERS = args.layers
     if args.impl == "reference":

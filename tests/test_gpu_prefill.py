@@ -90,8 +90,9 @@ def test_prefill_routed_vs_oracle(cuda, name, T_tok, K):
     assert max_step <= 1 and bad_codes <= n * F // 2000, (bad_ds, bad_codes, max_step)
 
 
-def test_prefill_dense_shared_gemma_vs_oracle(cuda):
-    cfg = synth.GEMMA
+@pytest.mark.parametrize("name", ["gemma", "qwen"])   # Q4_0 (Gemma) and Q8_0 (Qwen) dense shared experts
+def test_prefill_dense_shared_vs_oracle(cuda, name):
+    cfg = CFGS[name]
     H, FS = cfg["n_embd"], cfg["sh_n_ff"]
     layer = synth.make_layer(cfg, 31, n_expert=1)
     rng = np.random.default_rng(31)
@@ -100,21 +101,23 @@ def test_prefill_dense_shared_gemma_vs_oracle(cuda):
     Ls = T.native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, FS)
     sh = dev(layer["sh_blob"])
     xqd = T.quantize_q8_1_rows(dev(x))
-    h = T.moe_prefill_gu(Ls, sh, 0, None, 1, T_tok, xqd, None, act=cfg["sh_act"])
+    h = T.moe_prefill_gu(Ls, sh, 0, None, 1, T_tok, xqd, None, act=cfg.get("sh_act", cfg["act"]))
     out = T.moe_prefill_down(Ls, sh, 0, None, 1, T_tok, h)
     torch.cuda.synchronize()
     xq = xqd.cpu().numpy()
-    ref = np.stack([O.expert_ffn(cfg["sh_gu_type"], cfg["sh_d_type"], layer["sh_blob"], H, FS, xq[t], cfg["sh_act"])
+    ref = np.stack([O.expert_ffn(cfg["sh_gu_type"], cfg["sh_d_type"], layer["sh_blob"], H, FS, xq[t],
+                                 cfg.get("sh_act", cfg["act"]))
                     for t in range(T_tok)])
     err, cos = tol(out.cpu().numpy(), ref)
     assert err <= 1e-2 and cos >= 0.9999, (err, cos)
 
 
 def test_prefill_rejects_unsupported(cuda):
-    cfg = synth.QWEN   # Q8_0 routed weights: no prefill kernel (the reference's packs do not use them)
-    L = T.native_expert_layout(synth.T_Q8_0, synth.T_Q8_0, cfg["n_embd"], cfg["n_ff"])
+    # expert widths that do not fill the kernel's 64-value stages are refused (UNSUPPORTED), nothing is launched
+    H, F = 2048, 96
+    L = T.native_expert_layout(synth.T_Q4_0, synth.T_Q4_0, H, F)
     blobs = torch.zeros(int(L.bytes), dtype=torch.uint8, device="cuda")
-    xq = torch.zeros((4, cfg["n_embd"] // 32 * 36), dtype=torch.uint8, device="cuda")
+    xq = torch.zeros((4, H // 32 * 36), dtype=torch.uint8, device="cuda")
     with pytest.raises(T.TsbError, match="status -2"):
         T.moe_prefill_gu(L, blobs, int(L.bytes), None, 1, 4, xq)
 

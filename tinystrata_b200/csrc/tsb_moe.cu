@@ -826,6 +826,7 @@ static int pfx_launch_m(int wt, PfParams& pp, cudaStream_t s, DevInfo* di) {
         case T_Q4_K: return pfx_launch_t<MODE, T_Q4_K, A16>(pp, s, di);
         case T_Q6_K: return pfx_launch_t<MODE, T_Q6_K, A16>(pp, s, di);
         case T_IQ3_XXS: return pfx_launch_t<MODE, T_IQ3_XXS, A16>(pp, s, di);
+        case T_Q8_0: return pfx_launch_t<MODE, T_Q8_0, A16>(pp, s, di);
         default: return pfx_launch_t<MODE, T_IQ3_S, A16>(pp, s, di);
     }
 }
@@ -855,12 +856,12 @@ static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob
     if (!L || !blobs || n_rows < 0 || n_groups < 1 || n_groups > kPfMaxGroups)
         return fail(TSB_ERR_ARG, "moe_prefill: arguments");
     const int t = mode == PF_GU ? L->gu_type : L->d_type;
-    if (t != T_Q4_0 && t != T_Q4_K && t != T_Q6_K && t != T_IQ3_XXS && t != T_IQ3_S)
-        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)", t);
+    if (t != T_Q4_0 && t != T_Q8_0 && t != T_Q4_K && t != T_Q6_K && t != T_IQ3_XXS && t != T_IQ3_S)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)", t);
     if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 128)
         return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd and n_ff multiples of 64, at least 128");
     const int64_t k = mode == PF_GU ? L->n_embd : L->n_ff;   // super-block formats: the contraction in 256-value blocks
-    if (t != T_Q4_0 && k % 256) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: K-quant / i-quant rows of 256-value blocks");
+    if (t != T_Q4_0 && t != T_Q8_0 && k % 256) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: K-quant / i-quant rows of 256-value blocks");
     // Q4_0 rows are read in 4-byte words; the other formats' loaders take 2-byte aligned rows (Q6_K rows are 210 n / 256
     // bytes), Q4_K's 16-byte ones (144-byte blocks)
     const int64_t row = mode == PF_GU ? L->gu_row : L->d_row;

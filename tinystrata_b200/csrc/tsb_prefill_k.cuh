@@ -1,6 +1,7 @@
-// tsb_prefill_k.cuh - the prefill grouped expert products for the K-quant and i-quant weight formats (Q4_K, Q6_K,
-// IQ3_XXS, IQ3_S) on tcgen05.  The kernel has the shape of the Q4_0 kernel (tsb_prefill.cuh: producers, one MMA
-// thread, eight epilogue warps holding fp32 accumulators in registers); what changes is the weight side:
+// tsb_prefill_k.cuh - the prefill grouped expert products for the K-quant, i-quant and Q8_0 weight formats (Q4_K,
+// Q6_K, IQ3_XXS, IQ3_S; Q8_0 for the Qwen layer's dense shared expert) on tcgen05.  The kernel has the shape of the
+// Q4_0 kernel (tsb_prefill.cuh: producers, one MMA thread, eight epilogue warps holding fp32 accumulators in
+// registers); what changes is the weight side:
 //   * the producers decode each weight row's 64 values of a ring stage into exact fp16 integers -- Q4_K codes 0..15,
 //     Q6_K codes - 32, IQ3 grid bytes with their signs applied -- and stage the per-(row, 32-value block) scale terms
 //     the reference applies after its integer dot (src/kernels/cuda/iq_kernels.cu:188-236, 314-386, 523-553);
@@ -10,6 +11,7 @@
 //       Q6_K    acc += (d d_x) (sc_a S_a + sc_b S_b)                  (an exact integer in fp32)
 //       IQ3_XXS acc += (d d_x) ((ls S + S / 2) / 2)                   (C integer division, as the reference)
 //       IQ3_S   acc += ((d (1 + 2 sc)) d_x) S
+//       Q8_0    acc += (d d_x) S                                       (32-value blocks: int8 codes, one fp16 scale)
 // The activation side (q8_1 codes, exact in fp16) and the gate/up and down epilogues are the Q4_0 kernel's.
 #pragma once
 
@@ -29,6 +31,7 @@ template <> struct PxFmt<T_Q4_K> { static constexpr int kBytes = 144, kSplit = 1
 template <> struct PxFmt<T_Q6_K> { static constexpr int kBytes = 210, kSplit = 2; };
 template <> struct PxFmt<T_IQ3_XXS> { static constexpr int kBytes = 98, kSplit = 1; };
 template <> struct PxFmt<T_IQ3_S> { static constexpr int kBytes = 110, kSplit = 1; };
+template <> struct PxFmt<T_Q8_0> { static constexpr int kBytes = 34, kSplit = 1; };   // per 32 values
 
 // ------------------------------------------------------------------------------------------------ byte access
 // NW little-endian words from a 2-byte aligned address: aligned loads and funnel shifts.  Reads no aligned word past
@@ -87,7 +90,23 @@ __device__ __forceinline__ void px_stage_w(const uint8_t* wrow, int ks, uint8_t*
                                            const uint32_t* gxxs, const uint32_t* gs) {
     const int sb = ks >> 2, s = ks & 3;
     const uint8_t* base = wrow + (size_t) sb * PxFmt<WT>::kBytes;
-    if constexpr (WT == T_Q4_K) {
+    if constexpr (WT == T_Q8_0) {
+        // blocks 2 ks, 2 ks + 1: (d, 32 int8 codes) each, 68 bytes from a 2-byte aligned address
+        uint32_t w[17];
+        ldw<17>(wrow + (size_t) ks * 68, w);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+            const int o = 34 * hb;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = byte_of(w, o + 2 + 8 * c + k) ^ 0x80u;   // code + 128
+                *(uint4*) (tile + sw128(r, 4 * hb + c)) = pack8_unsigned(v, 1152.0f);
+            }
+            wt[(0 * 2 + hb) * kPfBN + r] = h2f(byte_of(w, o) | (byte_of(w, o + 1) << 8));
+        }
+    } else if constexpr (WT == T_Q4_K) {
         // d, dmin, scales[12], qs[128]: the stage's sub-blocks 2s, 2s+1 are the low / high nibbles of qs[32s .. +32)
         const uint4 hdr = __ldg((const uint4*) base);
         const uint4 qa = __ldg((const uint4*) (base + 16 + 32 * s)), qb = __ldg((const uint4*) (base + 32 + 32 * s));
