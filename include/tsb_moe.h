@@ -129,8 +129,8 @@ int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t
  * blob_stride in layout L; bounds null: one group of n_rows rows), h[row] = q8_1(act(gate . x, up . x)) with x the
  * q8_1 row row_tok ? row_tok[row] : row of x_q8_1 (n_embd / 32 blocks per row, as quantize_q8_1_rows writes it);
  * h_q8_1 holds n_rows x n_ff / 32 blocks.  The block dots are exact and scaled and summed in fp32 block after block,
- * as the reference's.  act as tsb_native_expert_grouped_act.  Q4_0 weights with block scales |d| <= 8; n_embd and
- * n_ff multiples of 64, at least 128.  Replaces the gate/up mmq::Context::run + mmq::swiglu + the re-quantisation of
+ * as the reference's.  act as tsb_native_expert_grouped_act.  Weights Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS or IQ3_S
+ * (L's gu_type); n_embd and n_ff multiples of 64, at least 128, and of 256 for the K-quant and i-quant formats.  Replaces the gate/up mmq::Context::run + mmq::swiglu + the re-quantisation of
  * the prompt path (src/prefill/moe_mmq.cu:334-384, 123-131). */
 int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
                        int n_groups, int n_rows, const void* x_q8_1, const int32_t* row_tok, void* h_q8_1, int act,
