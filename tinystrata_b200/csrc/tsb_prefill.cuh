@@ -34,7 +34,7 @@
 
 namespace tsb {
 
-constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 6, kPfSBuf = 3;
+constexpr int kPfBM = 128, kPfBN = 128, kPfBK = 64, kPfStages = 6, kPfSBuf = 4;
 constexpr int kPfProducerWarps = 4, kPfMmaWarp = 4, kPfEpiWarp0 = 5, kPfEpiWarps = 8, kPfWarps = 13;
 constexpr int kPfThreads = kPfWarps * 32;
 constexpr uint32_t kPfTileA = kPfBM * kPfBK * 2, kPfTileB = kPfBN * kPfBK * 2;   // 16 KB each
@@ -113,6 +113,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t addr, const float (&v)[32]) {
                    "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
                    "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
                  : "memory");
+}
+// Two columns of a block at once: a += (w dx) s lane by lane with the packed fp32 pipe instructions (mul.rn.f32x2,
+// fma.rn.f32x2: the same IEEE roundings as two scalar mul / fma pairs, half the instructions).
+__device__ __forceinline__ void fma2_scaled(float& a0, float& a1, float w0, float w1, float dx, float s0, float s1) {
+    asm("{\n .reg .b64 w, d, s, a;\n mov.b64 w, {%2, %3};\n mov.b64 d, {%4, %4};\n mov.b64 s, {%5, %6};\n"
+        " mov.b64 a, {%0, %1};\n mul.rn.f32x2 w, w, d;\n fma.rn.f32x2 a, w, s, a;\n mov.b64 {%0, %1}, a;\n}\n"
+        : "+f"(a0), "+f"(a1)
+        : "f"(w0), "f"(w1), "f"(dx), "f"(s0), "f"(s1));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -445,10 +453,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 w0 = dw4[8 * hh + j4];
-                        acc[32 * hh + 4 * j4 + 0] = fmaf(w0.x * dx, sv[4 * j4 + 0], acc[32 * hh + 4 * j4 + 0]);
-                        acc[32 * hh + 4 * j4 + 1] = fmaf(w0.y * dx, sv[4 * j4 + 1], acc[32 * hh + 4 * j4 + 1]);
-                        acc[32 * hh + 4 * j4 + 2] = fmaf(w0.z * dx, sv[4 * j4 + 2], acc[32 * hh + 4 * j4 + 2]);
-                        acc[32 * hh + 4 * j4 + 3] = fmaf(w0.w * dx, sv[4 * j4 + 3], acc[32 * hh + 4 * j4 + 3]);
+                        float* a = acc + 32 * hh + 4 * j4;
+                        fma2_scaled(a[0], a[1], w0.x, w0.y, dx, sv[4 * j4 + 0], sv[4 * j4 + 1]);
+                        fma2_scaled(a[2], a[3], w0.z, w0.w, dx, sv[4 * j4 + 2], sv[4 * j4 + 3]);
                     }
                 }
                 tc_fence_before();
