@@ -256,8 +256,9 @@ EPQ_METRIC = "EP prefill MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped IQ3_XXS/IQ3_
 def bench_ep_qwen(args):
     """C4: the Qwen3.6-35B-A3B-shaped layer (256 experts, IQ3_XXS gate/up, IQ3_S down, top-8 softmax, Q8_0 shared
     expert gated by a sigmoid of the 257th router row) over T = 65536 prompt tokens split evenly over the ranks
-    (strong scaling), experts sharded 256 / N per GPU, router logits skewed by a Zipf(1.1) prior over the experts
-    (log p_e added to expert e's logit) so that the expert load is imbalanced.  Per step: router GEMM, routing, q8_1,
+    (strong scaling), experts sharded 256 / N per GPU in cyclic placement (expert e on rank e % N: the skewed head
+    spreads over the ranks), router logits skewed by a Zipf(1.1) prior over the experts (log p_e added to expert
+    e's logit) so that the expert load is imbalanced.  Per step: router GEMM, routing, q8_1,
     dispatch / return all-to-alls over NCCL, local experts and the shared expert on the tensor cores, gated sum.
     Eager (host-synchronising counts), timed with CUDA events between barriers, max over ranks."""
     import datetime
@@ -281,8 +282,8 @@ def bench_ep_qwen(args):
     T = T_all // ws
     H, F, FS, K, E = cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
     per = E // ws
-    st = synth.device_layers(cfg, 1, seed=4, device=device)   # every rank draws the same layer, keeps its slice
-    blobs = st["blobs"][0][rank * per:(rank + 1) * per].contiguous()
+    st = synth.device_layers(cfg, 1, seed=4, device=device)   # every rank draws the same layer, keeps its experts
+    blobs = st["blobs"][0][rank::ws].contiguous()
     router, sh = st["routers"][0], st["sh_blobs"][0]
     del st
     L = TS.native_expert_layout(cfg["gu_type"], cfg["d_type"], H, F)
@@ -296,7 +297,7 @@ def bench_ep_qwen(args):
         lg = logits[:, :E] + zipf
         ids, w = TS.native_router_topk(lg.contiguous(), K)       # softmax top-8, renormalised (the Qwen router)
         xq = TS.quantize_q8_1_rows(x0)
-        out = ep_forward(xq, ids, w, E, H, fn)
+        out = ep_forward(xq, ids, w, E, H, fn, cyclic=True)
         hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xq, None, cfg["act"])
         shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
         return out.addcmul_(shared, torch.sigmoid(logits[:, E:E + 1]))
@@ -327,6 +328,7 @@ def bench_ep_qwen(args):
             "data": "synthetic (Zipf(1.1)-skewed router logits)",
             "config": {"workload": f"expert-parallel prefill, {T_all} tokens over {ws} GPU(s), {per} of {E} "
                                    "experts per GPU", "tokens": T_all, "tokens_per_gpu": T, "experts_per_gpu": per,
+                       "placement": "cyclic (expert e on rank e % N)",
                        "parallelism": f"ep{ws}",
                        "collectives": "NCCL all_to_all_single (counts, q8_1 rows, picks; fp32 partial rows back)"},
             "us_per_layer": ms * 1e3,

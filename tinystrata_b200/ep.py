@@ -1,10 +1,12 @@
-"""Expert-parallel prefill (the multi-GPU row of the expert path): experts [r E/G, (r+1) E/G) live on rank r, every rank
-routes its own tokens, and two all-to-all exchanges move the work (the layout TinyStrata's serving layer would shard
+"""Expert-parallel prefill (the multi-GPU row of the expert path): experts [r E/G, (r+1) E/G) live on rank r (block
+placement), or experts r, r + G, r + 2G, ... (cyclic placement: a popularity-ordered expert set -- a skewed router's
+head -- spreads over the ranks instead of landing on rank 0), every rank routes its own tokens, and two all-to-all
+exchanges move the work (the layout TinyStrata's serving layer would shard
 its prompt path with; the reference itself runs a single GPU, src/gemma4/engine.cpp:2436-2457 is the per-GPU body).
 
 One forward:
-  1. destinations: rank of each pick (expert // (E / G)); a token goes to a rank once, whatever number of its picks
-     live there (deduplicated), in token order;
+  1. destinations: rank of each pick (expert // (E / G), or expert % G when cyclic); a token goes to a rank once,
+     whatever number of its picks live there (deduplicated), in token order;
   2. counts exchange (all_to_all_single of G int64);
   3. dispatch exchange: the tokens' q8_1 rows and, per row, the local expert ids of its picks on that rank (-1 for the
      others) and their weights (0 for the others);
@@ -22,12 +24,18 @@ import torch.distributed as dist
 
 
 class EPPlan:
-    """Where each local token goes: per destination rank the tokens (ascending) and their picks on that rank."""
+    """Where each local token goes: per destination rank the tokens (ascending) and their picks on that rank (local
+    expert ids: the expert's index among its rank's experts)."""
 
-    def __init__(self, ids: torch.Tensor, w: torch.Tensor, n_expert: int, world: int):
+    def __init__(self, ids: torch.Tensor, w: torch.Tensor, n_expert: int, world: int, cyclic: bool = False):
         T, K = ids.shape
         per = n_expert // world
-        dest = torch.div(ids.long(), per, rounding_mode="floor")                     # [T, K]
+        if cyclic:
+            dest = torch.remainder(ids.long(), world)                                   # [T, K]
+            local = torch.div(ids.long(), world, rounding_mode="floor")
+        else:
+            dest = torch.div(ids.long(), per, rounding_mode="floor")
+            local = ids.long() - dest * per
         self.world = world
         self.per = per
         ranks = torch.arange(world, device=ids.device).view(world, 1, 1)
@@ -37,7 +45,7 @@ class EPPlan:
         toks = [torch.nonzero(mask[d], as_tuple=False).view(-1) for d in range(world)]
         self.send_tok = toks                                                          # per destination, ascending
         self.send_idx = torch.cat(toks) if T else torch.zeros(0, dtype=torch.long, device=ids.device)
-        lid = ids.long().unsqueeze(0) - ranks * per                                   # local ids on each rank
+        lid = local.unsqueeze(0).expand(world, T, K)                                  # local ids on each rank
         lid = torch.where(hit, lid, torch.full_like(lid, -1))
         wl = torch.where(hit, w.unsqueeze(0).expand(world, T, K), torch.zeros_like(w).unsqueeze(0).expand(world, T, K))
         self.send_ids = torch.cat([lid[d][toks[d]] for d in range(world)]).to(torch.int32)      # [S, K]
@@ -51,12 +59,12 @@ def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits, in_splits, group):
 
 
 def ep_forward(xq: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, n_expert: int, n_embd: int, expert_fn,
-               group=None) -> torch.Tensor:
+               group=None, cyclic: bool = False) -> torch.Tensor:
     """The routed part of the layer for this rank's T tokens: xq [T, row bytes] (uint8 q8_1 rows), ids / w [T, K] ->
     fp32 [T, n_embd].  expert_fn(rows uint8 [R, row bytes], ids int32 [R, K] (local expert, -1 = none), w [R, K]) ->
-    fp32 [R, n_embd]."""
+    fp32 [R, n_embd].  cyclic: expert e lives on rank e % G as local expert e // G (else on rank e // (E / G))."""
     world = dist.get_world_size(group)
-    plan = EPPlan(ids, w, n_expert, world)
+    plan = EPPlan(ids, w, n_expert, world, cyclic)
     dev = xq.device
     send_counts = plan.counts.to(torch.int64)
     recv_counts = torch.empty_like(send_counts)
