@@ -218,21 +218,21 @@ __device__ __forceinline__ void stage_q8_codes(const uint32_t (&blk)[9], uint8_t
     }
 }
 // Q4_0 centred nibbles q - 8 -> fp16 (exact) into chunks 4h..4h+3 of row r.  Values 0..15 of a block are the low
-// nibbles of bytes 0..15, values 16..31 the high nibbles; 0x6400 | q is the fp16 1024 + q, minus 1032 leaves q - 8.
+// nibbles of bytes 0..15, values 16..31 the high nibbles.  Four nibbles at a time: one mask leaves them as bytes, two
+// byte permutes put each under the fp16 exponent pattern 0x64 (1024 + q), one subtraction of 1032 per pair leaves q - 8.
 __device__ __forceinline__ void stage_q4_0(const uint32_t (&blk)[5], uint8_t* tile, int r, int h) {
     const half2 bias = __float2half2_rn(1032.0f);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {   // chunk c: values 8c..8c+7 (c < 2 low nibbles, c >= 2 high nibbles)
-        const uint32_t q0 = blk[1 + (c & 1) * 2], q1 = blk[2 + (c & 1) * 2];
-        const int sh = (c >> 1) * 4;
         uint32_t out[4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {   // values 2p, 2p+1: bytes 2p, 2p+1 of the 8 source bytes
-            const uint32_t x = (p < 2 ? q0 : q1) >> ((p & 1) * 16);
-            const uint32_t lo = (x >> sh) & 0xFu, hi = (x >> (8 + sh)) & 0xFu;
-            const uint32_t bits = 0x64006400u | lo | (hi << 16);
-            const half2 v = __hsub2(*(const half2*) &bits, bias);
-            out[p] = *(const uint32_t*) &v;
+        for (int k = 0; k < 2; ++k) {   // the chunk's source words: bytes 8 (c & 1) + 4k ..
+            const uint32_t w = blk[1 + (c & 1) * 2 + k];
+            const uint32_t b = (c >> 1 ? (w >> 4) : w) & 0x0F0F0F0Fu;
+            const uint32_t p0 = __byte_perm(b, 0x64646464u, 0x5140), p1 = __byte_perm(b, 0x64646464u, 0x7362);
+            const half2 v0 = __hsub2(*(const half2*) &p0, bias), v1 = __hsub2(*(const half2*) &p1, bias);
+            out[2 * k] = *(const uint32_t*) &v0;
+            out[2 * k + 1] = *(const uint32_t*) &v1;
         }
         *(uint4*) (tile + sw128(r, 4 * h + c)) = make_uint4(out[0], out[1], out[2], out[3]);
     }
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
         // previous stage is converted
         const int r = threadIdx.x;
         uint32_t it = 0;
-        PfRaw R;
+        PfRaw R, R2;
         for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
             int g, row0, row1, n0;
             tile_of(tile, g, row0, row1, n0);
@@ -324,25 +324,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                     if (j < p.N) wrow = base + (size_t) j * p.w_row;
                 }
             }
-            pf_load<A16, W16>(R, xrow, wrow, 0);
-            for (int ks = 0; ks < nks; ++ks, ++it) {
-                const PfRaw cur = R;
-                if (ks + 1 < nks) pf_load<A16, W16>(R, xrow, wrow, ks + 1);
+            // one ring stage from its raw bytes; false: a wait gave up
+            auto stage = [&](const PfRaw& cur, int ks) -> bool {
                 const int s = (int) (it % kPfStages);
                 if (it >= (uint32_t) kPfStages) {
                     const uint32_t par = ((it / kPfStages) - 1) & 1u;
                     const uint64_t t0 = globaltimer();
-                    bool ok = true;
                     while (!mbar_try_wait(&empty[s], par))
                         if (globaltimer() - t0 > kWaitNs || abort_flag) {
-                            ok = false;
-                            break;
+                            report_error(p.err, 0x501u);
+                            abort_flag = 1;
+                            return false;
                         }
-                    if (!ok) {
-                        report_error(p.err, 0x501u);
-                        abort_flag = 1;
-                        break;
-                    }
                 }
                 uint8_t* sa = smem + s * kPfStage;
                 uint8_t* sb = sa + kPfTileA;
@@ -375,7 +368,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfParams p) {
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
+                ++it;
+                return true;
+            };
+            // two raw buffers in turn: stage ks converts from one while stage ks + 1's bytes load into the other
+            pf_load<A16, W16>(R, xrow, wrow, 0);
+            bool ok = true;
+            for (int ks = 0; ks < nks && ok; ks += 2) {
+                if (ks + 1 < nks) pf_load<A16, W16>(R2, xrow, wrow, ks + 1);
+                ok = stage(R, ks);
+                if (ok && ks + 1 < nks) {
+                    if (ks + 2 < nks) pf_load<A16, W16>(R, xrow, wrow, ks + 2);
+                    ok = stage(R2, ks + 1);
+                }
             }
+            if (!ok) break;
         }
     } else if (warp == kPfMmaWarp) {
         // ------------------------------------------------------------------------ MMA issue
