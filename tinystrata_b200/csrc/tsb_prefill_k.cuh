@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm_x(PfParams p) {
         // thread r: activation row r (its q8_1 windows loaded a stage ahead) and weight row r of every stage
         const int r = threadIdx.x;
         uint32_t it = 0;
-        PfRaw R;
+        PfRaw R, R2;
         for (int tile = blockIdx.x; tile < n_tiles && !abort_flag; tile += gridDim.x) {
             int g, row0, row1, n0;
             tile_of(tile, g, row0, row1, n0);
@@ -320,25 +320,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm_x(PfParams p) {
                     if (j < p.N) wrow = base + (size_t) j * p.w_row;
                 }
             }
-            pf_load<A16, false>(R, xrow, nullptr, 0);
-            for (int ks = 0; ks < nks; ++ks, ++it) {
-                const PfRaw cur = R;
-                if (ks + 1 < nks) pf_load<A16, false>(R, xrow, nullptr, ks + 1);
+            // one ring stage; false: a wait gave up
+            auto stage = [&](const PfRaw& cur, int ks) -> bool {
                 const int s = (int) (it % kPxStages);
                 if (it >= (uint32_t) kPxStages) {
                     const uint32_t par = ((it / kPxStages) - 1) & 1u;
                     const uint64_t t0 = globaltimer();
-                    bool ok = true;
                     while (!mbar_try_wait(&empty[s], par))
                         if (globaltimer() - t0 > kWaitNs || abort_flag) {
-                            ok = false;
-                            break;
+                            report_error(p.err, 0x511u);
+                            abort_flag = 1;
+                            return false;
                         }
-                    if (!ok) {
-                        report_error(p.err, 0x511u);
-                        abort_flag = 1;
-                        break;
-                    }
                 }
                 uint8_t* sa = smem + s * kPxStage;
                 uint8_t* sb = sa + kPfTileA;
@@ -374,7 +367,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm_x(PfParams p) {
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
+                ++it;
+                return true;
+            };
+            // two raw activation buffers in turn: stage ks converts from one while stage ks + 1's bytes load
+            pf_load<A16, false>(R, xrow, nullptr, 0);
+            bool ok = true;
+            for (int ks = 0; ks < nks && ok; ks += 2) {
+                if (ks + 1 < nks) pf_load<A16, false>(R2, xrow, nullptr, ks + 1);
+                ok = stage(R, ks);
+                if (ok && ks + 1 < nks) {
+                    if (ks + 2 < nks) pf_load<A16, false>(R, xrow, nullptr, ks + 2);
+                    ok = stage(R2, ks + 1);
+                }
             }
+            if (!ok) break;
         }
     } else if (warp == kPfMmaWarp) {
         // ------------------------------------------------------------------------ MMA issue
