@@ -25,9 +25,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_LAYERS = 40   # --layers changes it for profiling captures only (a smaller device footprint); the bench is 40
-# DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch
-# (profiles/k_decode_layers_qwen_decode_T1_4layers_full.md: 61.77 MB per launch); traffic grows with the layer count,
-# so a launch of N layers moves N times this.
+# DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch (61.77 MB
+# per launch); traffic grows with the layer count, so a launch of N layers moves N times this.
 TRAFFIC_PER_LAYER_T1 = 61.77e6 / 4
 METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
 
@@ -123,26 +122,56 @@ def reference_arm(args):
     return 0
 
 
-def build_stack(cfg, T, device, seed=1):
+def decode_priors(cfg, T, device):
+    """C1 at T > 1: each token's top-8 distinct and disjoint across the step's tokens (T * 8 distinct experts per
+    layer).  The routing prior adds 30 to the logits of token t's experts {(8 t + k + 37 l) mod 256} in layer l (the
+    natural logits spread about 1 on RMS-normed inputs), through the decode path's logit_prior input; T = 1 routes
+    without a prior.  Returns [L][T][E] fp32 or None."""
     import torch
-    import tinystrata_b200 as TS
-    from tinystrata_b200 import synth
-    st = synth.device_layers(cfg, N_LAYERS, seed, device)
-    H, E, K = cfg["n_embd"], cfg["n_expert"], cfg["n_used"]
-    # routing made disjoint across the step's tokens: token t's experts are {8t .. 8t+7} (mod 256), planted in every
-    # layer's router on input dimension d_t, and the inputs carry a spike there large enough to survive 40 layers
-    dims = [(7 + 61 * t) % H for t in range(T)]
+    if T == 1:
+        return None
+    E, K = cfg["n_expert"], cfg["n_used"]
+    pr = torch.zeros((N_LAYERS, T, E), dtype=torch.float32)
     for l in range(N_LAYERS):
         for t in range(T):
             for k in range(K):
-                st["routers"][l, (t * K + k) % E, dims[t]] = 1.0 + 0.01 * k
-    layers = [TS.MoELayer(cfg, st["blobs"][l], st["routers"][l], st["sh_blobs"][l], max_tokens=max(T, 1))
-              for l in range(N_LAYERS)]
-    rng = np.random.default_rng(seed)
-    x0 = rng.normal(0, 1, size=(T, H)).astype(np.float32)
-    for t in range(T):
-        x0[t, dims[t]] = 1e8
-    return st, layers, x0
+                pr[l, t, (t * K + k + 37 * l) % E] = 30.0
+    return pr.to(device)
+
+
+def verify_decode(cfg, D, layers, x0_dev, priors, stream):
+    """The fused step checked layer by layer (teacher-forced): layer l of the layer-by-layer entry points (MoELayer,
+    whose pieces the GPU parity tests pin to the reference's kernels) runs on the fused step's own input to layer l
+    (x after layer l - 1, recorded by the step), and its routing and MoE output (x_l - x_{l-1}) are compared with the
+    fused step's.  Tolerance as the layer parity tests: max-abs <= 1e-2 of the output RMS, cosine >= 0.9999."""
+    import torch
+    import tinystrata_b200 as TS
+    T, H = x0_dev.shape
+    with torch.cuda.stream(stream):
+        x = x0_dev.clone()
+        D.forward(x, stream=stream)
+    stream.synchronize()
+    assert D.error() == 0 and TS.device_error() == 0, D.error_detail
+    worst, min_cos, same = 0.0, 1.0, True
+    h = torch.empty((T, H), device=x0_dev.device)
+    hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=x0_dev.device)
+    for l, M in enumerate(layers):
+        xin = x0_dev if l == 0 else D.x_rec[l - 1]
+        with torch.cuda.stream(stream):
+            x1 = xin.clone()
+            TS.rms_norm_q8_1(x1, h, hq, stream=stream)
+            M.forward(x1, h, hq, stream=stream, prior=priors[l] if priors is not None else None)
+        stream.synchronize()
+        ref = (x1 - xin).double()
+        got = (D.x_rec[l] - xin).double()
+        rms = float(ref.pow(2).mean().sqrt())
+        err = float((got - ref).abs().max()) / rms
+        cos = float((got * ref).sum() / (got.norm() * ref.norm()))
+        worst, min_cos = max(worst, err), min(min_cos, cos)
+        same &= bool(torch.equal(D.ids[l], M.ids[:T]))
+    assert torch.isfinite(D.x_rec).all(), "non-finite layer output"
+    return {"layers": len(layers), "max_abs_over_rms": worst, "min_cosine": min_cos, "same_routing": same,
+            "teacher_forced": True, "tolerance": {"max_abs_over_rms": 1e-2, "cosine": 0.9999}}
 
 
 PREFILL_METRIC = "MoE-layer tokens/s (prefill, Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192)"
@@ -427,6 +456,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--impl", default="tsb", choices=["tsb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="only the headline token count (profiling captures)")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen"],
@@ -444,7 +474,13 @@ def main():
     N_LAYERS = args.layers
     if args.impl == "reference":
         return reference_arm(args)
+    return bench_decode(args)
 
+
+def bench_decode(args):
+    """C1: the Qwen-shaped decode step through 40 resident layers (the headline line), at T = args.tokens, plus the
+    other C1 token counts (2, 4, 16) as extra keys.  Every configuration is verified layer by layer before it is
+    timed; a broken tolerance or routing ends the run with an error instead of a number."""
     import torch
     import torch.distributed as dist
     import tinystrata_b200 as TS
@@ -461,74 +497,22 @@ def main():
         if ws > 1:
             dist.barrier()
 
+    def max_over_ranks(v):
+        if ws > 1:
+            t = torch.tensor([v], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return v
+
     cfg = synth.QWEN
-    T, H, K, E = args.tokens, cfg["n_embd"], cfg["n_used"], cfg["n_expert"]
-    st, layers, x0 = build_stack(cfg, T, device)
-    torch.cuda.synchronize()
-    x = torch.empty((T, H), device=device)
-    h = torch.empty((T, H), device=device)
-    hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
-    x0_dev = torch.from_numpy(x0).to(device)
-    x0_host = torch.from_numpy(x0).pin_memory()
-    out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
-
+    H, K, E = cfg["n_embd"], cfg["n_used"], cfg["n_expert"]
+    st = synth.device_layers(cfg, N_LAYERS, 1, device)
+    layers = [TS.MoELayer(cfg, st["blobs"][l], st["routers"][l], st["sh_blobs"][l], max_tokens=16)
+              for l in range(N_LAYERS)]
+    x_c1 = synth.rms_normed(np.random.default_rng(1), 16, H)   # C1 inputs: RMS-normed N(0, 1), seed 1
     stream = torch.cuda.Stream(device)
-    D = TS.DecodeStack(cfg, st["blobs"], st["routers"], st["sh_blobs"], n_tok=T)
-    torch.cuda.synchronize()
-
-    # verification pass (eager, untimed): the fused step against the layer-by-layer entry points, routing taken
-    with torch.cuda.stream(stream):
-        x.copy_(x0_dev)
-        TS.rms_norm_q8_1(x, h, hq, stream=stream)
-        for M in layers:
-            M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream)
-        x_layerwise = x.clone()
-        x.copy_(x0_dev)
-        D.forward(x, stream=stream)
-    stream.synchronize()
-    assert D.error() == 0 and TS.device_error() == 0
-    assert torch.isfinite(x).all(), "non-finite layer output"
-    rel = float(((x - x_layerwise).abs().max() / x_layerwise.pow(2).mean().sqrt()).item())
-    same_routing = all(torch.equal(D.ids[l], M.ids[:T]) for l, M in enumerate(layers))
-    distinct = [int(torch.unique(D.ids[l]).numel()) for l in range(N_LAYERS)]
-    L, Ls = layers[0].L, layers[0].Ls
-    bytes_layer = [d * L.bytes + Ls.bytes + (E + 1) * H * 4 for d in distinct]
-    alg_bytes_per_layer = float(np.mean(bytes_layer))
-
-    if args.trace:
-        with torch.cuda.stream(stream):
-            x.copy_(x0_dev)
-        stream.synchronize()
-        tr = D.trace(x, stream=stream).double()
-        names = ["start", "P0", "P1", "bar1", "route", "P2", "bar2", "P3", "bar3", "pr:P1", "pr:route", "pr:P2",
-                 "pr:P3"]
-        rows = []
-        for l in range(1, N_LAYERS):
-            t0 = tr[l, 0].min()
-            rows.append([((tr[l, e] - t0) / 1e3).mean().item() for e in range(13)] +
-                        [((tr[l, e] - t0) / 1e3).max().item() for e in range(13)])
-        m = np.array(rows).mean(0)
-        print("phase (us from layer start): " + "  ".join(f"{n}={m[i]:.2f}/{m[13 + i]:.2f}" for i, n in
-                                                        enumerate(names)), file=sys.stderr, flush=True)
-
-    def fused_step():
-        x.copy_(x0_dev)
-        D.forward(x, stream=stream)
-
-    def layerwise_step():
-        x.copy_(x0_dev)
-        TS.rms_norm_q8_1(x, h, hq, stream=stream)
-        for M in layers:
-            M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream)
-
-    graphs = {}
-    for name, fn in (("fused", fused_step), ("layerwise", layerwise_step)):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g, stream=stream):
-                fn()
-        graphs[name] = g
-    stream.synchronize()
+    L0, Ls = layers[0].L, layers[0].Ls
+    peak, peak_kind = peaks()
 
     def timed(g, n):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -540,59 +524,131 @@ def main():
         stream.synchronize()
         return e0.elapsed_time(e1) / n
 
-    # warm-up, then the device-timed region (inputs resident, 12.3 GB of weights >> L2)
-    timed(graphs["fused"], max(3, args.warmup))
-    barrier()
-    torch.cuda.synchronize()
-    with Clocks(local) as clk:
-        ms = timed(graphs["fused"], args.steps)
-    torch.cuda.synchronize()
-    barrier()
-    assert D.error() == 0
-    if ws > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    us_layer = ms * 1e3 / N_LAYERS
-    value = ws * T / (us_layer * 1e-6)
-
-    # end to end: host input -> device, the fused step, device -> host, every step
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(args.steps):
-            x.copy_(x0_host, non_blocking=True)
-            D.forward(x, stream=stream)
-            out_host.copy_(x, non_blocking=True)
-        e1.record(stream)
-    stream.synchronize()
-    barrier()
-    ms_e2e = e0.elapsed_time(e1) / args.steps
-    if ws > 1:
-        t = torch.tensor([ms_e2e], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
-    e2e_value = ws * T / (ms_e2e * 1e3 / N_LAYERS * 1e-6)
-
-    # the dominant (and only) kernel alone, CUDA events on its stream: k_decode_layers over the 40 layers
-    kms = []
-    with torch.cuda.stream(stream):
-        for rep in range(4):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    def point(T, headline):
+        priors = decode_priors(cfg, T, device)
+        x0_dev = torch.from_numpy(x_c1[:T].copy()).to(device)
+        Dv = TS.DecodeStack(cfg, st["blobs"], st["routers"], st["sh_blobs"], n_tok=T, priors=priors, record_x=True)
+        check = verify_decode(cfg, Dv, layers, x0_dev, priors, stream)
+        del Dv
+        if not (check["same_routing"] and check["max_abs_over_rms"] <= 1e-2 and check["min_cosine"] >= 0.9999):
+            raise SystemExit(f"decode T={T}: the fused step does not match the layer-by-layer path: {check}")
+        D = TS.DecodeStack(cfg, st["blobs"], st["routers"], st["sh_blobs"], n_tok=T, priors=priors)
+        x = torch.empty((T, H), device=device)
+        with torch.cuda.stream(stream):
             x.copy_(x0_dev)
-            a.record(stream)
             D.forward(x, stream=stream)
-            b.record(stream)
-            kms.append((a, b))
-    stream.synchronize()
-    k_avg_ms = float(np.mean([a.elapsed_time(b) for a, b in kms[1:]]))
-    k_bytes = float(np.sum(bytes_layer))
-    peak, peak_kind = peaks()
-    k_gbs = k_bytes / (k_avg_ms * 1e-3) / 1e9
-    layerwise_us = timed(graphs["layerwise"], max(3, args.steps // 2)) * 1e3 / N_LAYERS
-    gpu_launches = args.steps   # one k_decode_layers per step
-    gu_avg_ms = k_avg_ms
+        stream.synchronize()
+        distinct = [int(torch.unique(D.ids[l]).numel()) for l in range(N_LAYERS)]
+        bytes_layer = [d * L0.bytes + Ls.bytes + (E + 1) * H * 4 for d in distinct]
+        if headline and args.trace:   # per-phase timeline of the fused kernel (mean / max over CTAs, us from start)
+            with torch.cuda.stream(stream):
+                x.copy_(x0_dev)
+            stream.synchronize()
+            tr = D.trace(x, stream=stream).double()
+            names = ["start", "P0", "P1", "routed", "sh_q", "P2", "hq", "P3", "end", "logits_in", "topk", "-", "-"]
+            rows = []
+            for l in range(1, N_LAYERS):
+                t0 = tr[l, 0].min()
+                rows.append([((tr[l, e] - t0) / 1e3).mean().item() for e in range(13)] +
+                            [((tr[l, e] - t0) / 1e3).max().item() for e in range(13)])
+            m = np.array(rows).mean(0)
+            print("phase (us from layer start): " + "  ".join(f"{n}={m[i]:.2f}/{m[13 + i]:.2f}" for i, n in
+                                                            enumerate(names)), file=sys.stderr, flush=True)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                x.copy_(x0_dev)
+                D.forward(x, stream=stream)
+        stream.synchronize()
+        timed(g, max(3, args.warmup))
+        barrier()
+        torch.cuda.synchronize()
+        clk = Clocks(local) if headline else None
+        if clk:
+            clk.__enter__()
+        ms = timed(g, args.steps)
+        if clk:
+            clk.__exit__()
+        torch.cuda.synchronize()
+        barrier()
+        assert D.error() == 0 and TS.device_error() == 0
+        ms = max_over_ranks(ms)
+        us_layer = ms * 1e3 / N_LAYERS
+        res = {"tokens": T, "us_per_layer": us_layer, "tokens_per_s": ws * T / (us_layer * 1e-6),
+               "ms_per_step": ms, "distinct_experts_per_layer": float(np.mean(distinct)),
+               "layer_algorithmic_bytes": float(np.mean(bytes_layer)),
+               "hbm_frac": float(np.mean(bytes_layer)) / (us_layer * 1e-6) / 1e9 / peak, "verify": check}
+        if not headline:
+            del g
+            return res
+        res["clocks"] = clk.summary()
+        # end to end through the public API: pinned host x in, the fused step, x back to the host, every step
+        x0_host = torch.from_numpy(x_c1[:T].copy()).pin_memory()
+        out_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                x.copy_(x0_host, non_blocking=True)
+                D.forward(x, stream=stream)
+                out_host.copy_(x, non_blocking=True)
+            e1.record(stream)
+        stream.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        res["e2e"] = {"value": ws * T / (ms_e2e * 1e3 / N_LAYERS * 1e-6), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                      "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)}
+        # the dominant (and only) kernel alone, CUDA events on its stream: k_decode_layers over the 40 layers
+        kms = []
+        with torch.cuda.stream(stream):
+            for rep in range(4):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                x.copy_(x0_dev)
+                a.record(stream)
+                D.forward(x, stream=stream)
+                b.record(stream)
+                kms.append((a, b))
+        stream.synchronize()
+        k_avg_ms = float(np.mean([a.elapsed_time(b) for a, b in kms[1:]]))
+        k_bytes = float(np.sum(bytes_layer))
+        k_gbs = k_bytes / (k_avg_ms * 1e-3) / 1e9
+        res["roofline"] = {"bound": "hbm", "kernel": "k_decode_layers (fused decode step, 40 layers)",
+                           "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak, "peak_kind": peak_kind,
+                           "traffic": TRAFFIC_PER_LAYER_T1 * N_LAYERS if T == 1 else None,
+                           "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer capture of "
+                                             "k_decode_layers, scaled to the launch's layers" if T == 1 else None,
+                           "algorithmic_bytes_per_launch": k_bytes, "avg_launch_ms": k_avg_ms}
+
+        def layerwise_step():
+            x.copy_(x0_dev)
+            h = torch.empty((T, H), device=device)
+            hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
+            TS.rms_norm_q8_1(x, h, hq, stream=stream)
+            for l, M in enumerate(layers):
+                M.forward(x, h, hq, h_next=h, hq_next=hq, stream=stream,
+                          prior=priors[l] if priors is not None else None)
+
+        gl = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(gl, stream=stream):
+                layerwise_step()
+        stream.synchronize()
+        res["layerwise_us_per_layer"] = timed(gl, max(3, args.steps // 2)) * 1e3 / N_LAYERS
+        del g, gl
+        return res
+
+    T = args.tokens
+    head = point(T, headline=True)
+    sweep = {}
+    if not args.no_sweep:
+        for Tx in (1, 2, 4, 16):
+            if Tx != T:
+                r = point(Tx, headline=False)
+                sweep[f"T={Tx}"] = {k: r[k] for k in ("us_per_layer", "tokens_per_s", "hbm_frac",
+                                                      "distinct_experts_per_layer", "layer_algorithmic_bytes")}
+                sweep[f"T={Tx}"]["verify"] = {k: r["verify"][k] for k in ("max_abs_over_rms", "min_cosine",
+                                                                         "same_routing")}
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
@@ -602,37 +658,29 @@ def main():
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
     if rank == 0:
-        clocks = clk.summary()
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 dp4a (q8_1 x IQ3_XXS / Q8_0), fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"decode T={T} through 40 resident Qwen3.6-35B-A3B-shaped MoE layers",
                        "model": "qwen3.6-35b-a3b-shaped MoE layer x40", "tokens_per_step": T, "layers": N_LAYERS,
                        "hidden": H, "experts": E, "top_k": K, "n_ff": cfg["n_ff"], "routed": "IQ3_XXS",
                        "shared": "Q8_0", "parallelism": f"replicas x{ws}",
-                       "distinct_experts_per_layer": float(np.mean(distinct)),
+                       "inputs": "RMS-normed N(0,1), seed 1" + ("" if T == 1 else "; routing prior: disjoint experts"),
+                       "distinct_experts_per_layer": head["distinct_experts_per_layer"],
                        "l2": "inputs larger than L2 (12.3 GB of expert weights, 40 distinct layers per step)"},
-            "us_per_layer": us_layer,
-            "layer_hbm_gbs": alg_bytes_per_layer / (us_layer * 1e-6) / 1e9,
-            "layerwise_us_per_layer": layerwise_us,
-            "fused_vs_layerwise": {"max_abs_over_rms": rel, "same_routing": same_routing},
-            "roofline": {"bound": "hbm", "kernel": "k_decode_layers (fused decode step, 40 layers)",
-                         "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
-                         "peak_kind": peak_kind,
-                         "traffic": TRAFFIC_PER_LAYER_T1 * N_LAYERS if T == 1 else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4-layer capture scaled "
-                                           "to the launch's layers" if T == 1 else None,
-                         "algorithmic_bytes_per_launch": k_bytes,
-                         "avg_launch_ms": k_avg_ms, "layer_algorithmic_bytes": alg_bytes_per_layer},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": ms_e2e,
-                    "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
-            "gpu_launches": gpu_launches,
-            "clocks": clocks,
+            "us_per_layer": head["us_per_layer"],
+            "layer_hbm_gbs": head["layer_algorithmic_bytes"] / (head["us_per_layer"] * 1e-6) / 1e9,
+            "layerwise_us_per_layer": head["layerwise_us_per_layer"],
+            "verify": head["verify"],
+            "roofline": head["roofline"],
+            "e2e": head["e2e"],
+            "gpu_launches": args.steps,   # one k_decode_layers per step
+            "clocks": head["clocks"],
             "cpu_baseline": cpu,
+            "decode_sweep": sweep,
         }
         print(json.dumps(line), flush=True)
-    del graphs
     if ws > 1:
         dist.destroy_process_group()
     return 0

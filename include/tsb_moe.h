@@ -45,9 +45,15 @@ typedef struct tsb_expert_layout {
 int tsb_moe_abi_version(void);
 /* The calling thread's last error message ("" when none). */
 const char* tsb_last_error(void);
-/* The current device's error word: non-zero when a kernel's bounded wait gave up (the kernel then returned early).
- * `clear` resets it.  Reads device memory (synchronous). */
+/* The current device's error word: non-zero when a kernel's bounded wait gave up (the kernel then returned early) or
+ * a device-side count exceeded the capacity the caller passed (the kernel clamped it).  `clear` resets it.  Reads
+ * device memory (synchronous).  The word is a module global of the library, zero when it loads: the library's first
+ * call on a device looks up its address (and may load the module), so make that first call outside stream capture. */
 int tsb_device_error(unsigned* code, int clear);
+/* The bound of every spin-wait in this library's kernels on the current device (default 2 s, accepted 1e5 .. 6e10 ns):
+ * a wait that runs past it records its site in the error word and the kernel returns early.  Synchronous; set it outside
+ * stream capture.  No counterpart in the reference (its kernels do not wait on one another). */
+int tsb_set_wait_limit_ns(uint64_t ns);
 
 /* --------------------------------------------------------------------------------------------- formats */
 /* Replaces iq_supported / iq_row_bytes (iq_kernels.hpp:17-21). */
@@ -115,11 +121,13 @@ int tsb_native_expert_grouped_act(const tsb_expert_layout* L, const uint64_t* gr
 /* tsb_native_expert_grouped (SwiGLU) without a caller scratch buffer: the hidden vectors live in a fixed 1 MiB device
  * array inside this library (cap_entries * n_ff * 4 bytes, rounded up to 256, must fit: 128 entries at n_ff 2048;
  * larger calls return TSB_ERR_WORKSPACE and launch nothing).  For callers that hold no workspace and must not
- * allocate one on the call path.  The array and the call's bounded-wait error word start at zero when the module loads;
- * the hidden vectors need no clearing between calls.  There is ONE array per device: calls that overlap in time on a
- * device (other streams or threads) race on it.  Its address is looked up once per device with cudaGetSymbolAddress
- * at the first call, which may load the module: make that first call outside any stream capture.  No counterpart in
- * the reference (native_expert_grouped, iq_kernels.hpp:75-78, always takes the caller's scratch). */
+ * allocate one on the call path.  The array starts at zero when the module loads; the hidden vectors need no clearing
+ * between calls.  A bounded wait that gives up is recorded in the device error word (tsb_device_error), as for every
+ * other entry point.  There is ONE array per device: calls that overlap in time on a device (other streams or threads)
+ * race on it.  Its address is looked up once per device with cudaGetSymbolAddress at the first call, which may load
+ * the module: make that first call outside any stream capture; the looked-up address does not survive a
+ * cudaDeviceReset.  No counterpart in the reference (native_expert_grouped, iq_kernels.hpp:75-78, always takes the
+ * caller's scratch). */
 int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t* grp_ptr, const int32_t* grp_start,
                                       const int32_t* n_groups, const int32_t* ent_dst, const int32_t* ent_tok,
                                       int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, float* out,
@@ -167,6 +175,8 @@ typedef struct tsb_decode_layer {
     const void* blobs;
     const float* router;
     const void* sh_blob;
+    const float* logit_prior;   /* optional [n_tok][n_expert] fp32 added to the router logits before the softmax (an
+                                   additive routing prior, e.g. a benchmark's fixed expert choice); null: none */
 } tsb_decode_layer;
 
 typedef struct tsb_decode_desc {
@@ -182,11 +192,12 @@ uint64_t tsb_moe_decode_workspace_bytes(const tsb_decode_desc* d);
 /* Every layer's MoE block for n_tok decode tokens in one persistent launch (one CTA per SM, cooperative):
  * per layer h = rms(x), router GEMV, softmax top-k, grouping, routed and shared experts, and x += the gated combine
  * (q36_engine.cu:2821-2925 with k_moe_out_small, per layer).  x: [n_tok][n_embd] fp32, in / out.  layers: a DEVICE
- * array of n_layers tsb_decode_layer.  ids_rec / w_rec (optional, [n_layers][n_tok][n_used]) record the routing.
+ * array of n_layers tsb_decode_layer.  ids_rec / w_rec (optional, [n_layers][n_tok][n_used]) record the routing and
+ * x_rec (optional, [n_layers][n_tok][n_embd]) x after every layer (a step that checks itself layer by layer).
  * Supported: IQ3_XXS routed experts (n_ff 512), 256 experts, Q8_0 shared expert, SwiGLU.  Replaces the per-layer
  * sequence f32mm + route_group + native_expert_grouped + shared expert + moe_end of the Qwen3.6 engine. */
 int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* layers, float* x, int32_t* ids_rec,
-                          float* w_rec, void* workspace, uint64_t ws_bytes, void* stream);
+                          float* w_rec, float* x_rec, void* workspace, uint64_t ws_bytes, void* stream);
 /* The decode kernel's error record in `workspace`: code[0] non-zero when a bounded wait gave up (its site), code[1..4]
  * that wait's context (unit sequence and layer, producer progress, claim counter, CTA, raw barrier words).  `code`
  * holds 128 words.
@@ -198,6 +209,10 @@ const char* tsb_decode_last_error(void);
  * u64) at each phase boundary of every layer (consumer stamps 0-8, producer stamps 9-12, see tsb_decode.cuh); null
  * turns it off.  Process-wide; a captured graph keeps the buffer it was captured with. */
 int tsb_moe_decode_set_trace(unsigned long long* buf);
+/* Tests of the bounded waits: launches made after this call have CTA withhold_cta - 1 skip publishing its layer-0
+ * router logits, so every other CTA's wait for them runs out (their site lands in the error record); 0 turns it off.
+ * Process-wide.  No counterpart in the reference. */
+int tsb_moe_decode_set_debug(int withhold_cta);
 
 /* --------------------------------------------------------------------------------------------- test hook */
 /* The per-call integer sums and float values of one weight row (n values) against one q8_1 activation, as the

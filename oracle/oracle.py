@@ -29,10 +29,16 @@ _i32 = C.c_int32
 _f = C.c_float
 
 
+def reference_dir() -> str:
+    """The TinyStrata source tree the `ref` builds compile from: $REF when set, else a `reference` directory beside
+    this repository (the same rule as oracle/Makefile)."""
+    return os.environ.get("REF") or os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
+
+
 def build(ref: bool = True) -> None:
     """make the C restatement, and the reference CPU kernels when the reference tree is present."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if ref and os.path.isdir(os.environ.get("REF", "/root/reference")):
+    if ref and os.path.isdir(reference_dir()):
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
 
 

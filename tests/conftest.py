@@ -20,7 +20,8 @@ def pytest_configure(config):
 @pytest.fixture(scope="session", autouse=True)
 def _oracle_built():
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "all"], check=True)
-    if os.path.isdir("/root/reference") and not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libtsb_ref_cpu.so")):
+    from oracle.oracle import reference_dir
+    if os.path.isdir(reference_dir()) and not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libtsb_ref_cpu.so")):
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref"], check=True)
     yield
 

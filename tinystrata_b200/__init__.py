@@ -25,7 +25,7 @@ class TsbError(RuntimeError):
 
 class DecodeLayer(C.Structure):
     """tsb_decode_layer: device pointers of one layer for the fused decode path."""
-    _fields_ = [("blobs", C.c_void_p), ("router", C.c_void_p), ("sh_blob", C.c_void_p)]
+    _fields_ = [("blobs", C.c_void_p), ("router", C.c_void_p), ("sh_blob", C.c_void_p), ("logit_prior", C.c_void_p)]
 
 
 class DecodeDesc(C.Structure):
@@ -77,10 +77,12 @@ SIGNATURES = {
     "tsb_native_expert_set_phase": (C.c_int, [C.c_int]),
     "tsb_debug_row_calls": (C.c_int, [C.c_int, _p, _p, _i64, _p, _p, _p]),
     "tsb_moe_decode_workspace_bytes": (_u64, [C.POINTER(DecodeDesc)]),
-    "tsb_moe_decode_layers": (C.c_int, [C.POINTER(DecodeDesc), _p, _p, _p, _p, _p, _u64, _p]),
+    "tsb_moe_decode_layers": (C.c_int, [C.POINTER(DecodeDesc), _p, _p, _p, _p, _p, _p, _u64, _p]),
     "tsb_moe_decode_error": (C.c_int, [C.POINTER(DecodeDesc), _p, _p]),
     "tsb_decode_last_error": (C.c_char_p, []),
     "tsb_moe_decode_set_trace": (C.c_int, [_p]),
+    "tsb_moe_decode_set_debug": (C.c_int, [C.c_int]),
+    "tsb_set_wait_limit_ns": (C.c_int, [_u64]),
 }
 
 
@@ -313,6 +315,17 @@ def debug_row_calls(ggml_type: int, row, x_q8_1, n: int, stream=None):
     return s, v
 
 
+def set_wait_limit_ns(ns: int):
+    """The bound of every spin-wait in the library's kernels on the current device (default 2e9 ns)."""
+    _check(lib().tsb_set_wait_limit_ns(int(ns)), "set_wait_limit_ns")
+
+
+def decode_set_debug(withhold_cta: int):
+    """Tests of the bounded waits: CTA withhold_cta - 1 of later fused-decode launches skips publishing its layer-0
+    router logits (0 turns it off)."""
+    _check(lib().tsb_moe_decode_set_debug(int(withhold_cta)), "moe_decode_set_debug")
+
+
 def device_error(clear: bool = True) -> int:
     code = C.c_uint(0)
     _check(lib().tsb_device_error(C.byref(code), int(clear)), "device_error")
@@ -321,9 +334,12 @@ def device_error(clear: bool = True) -> int:
 
 class DecodeStack:
     """The fused decode path over n_layers resident layers: one persistent launch per step
-    (tsb_moe_decode_layers).  blobs [L][E][bytes] uint8, routers [L][E + 1][H] fp32, sh_blobs [L][bytes] uint8."""
+    (tsb_moe_decode_layers).  blobs [L][E][bytes] uint8, routers [L][E + 1][H] fp32, sh_blobs [L][bytes] uint8,
+    priors (optional) [L][n_tok][E] fp32 added to the router logits.  record: keep every layer's routing (ids, w);
+    record_x: also x after every layer (x_rec [L][n_tok][H])."""
 
-    def __init__(self, cfg: dict, blobs, routers, sh_blobs, n_tok: int, eps: float = 1e-6, record: bool = True):
+    def __init__(self, cfg: dict, blobs, routers, sh_blobs, n_tok: int, eps: float = 1e-6, record: bool = True,
+                 priors=None, record_x: bool = False):
         import torch
         self.cfg = cfg
         L = blobs.shape[0]
@@ -331,19 +347,20 @@ class DecodeStack:
                                cfg["n_used"], cfg["sh_n_ff"], cfg["gu_type"], cfg["d_type"], cfg["sh_gu_type"],
                                cfg["sh_d_type"], eps)
         dev = blobs.device
-        tab = torch.tensor([[blobs[l].data_ptr(), routers[l].data_ptr(), sh_blobs[l].data_ptr()] for l in range(L)],
-                           dtype=torch.int64)
+        tab = torch.tensor([[blobs[l].data_ptr(), routers[l].data_ptr(), sh_blobs[l].data_ptr(),
+                             priors[l].data_ptr() if priors is not None else 0] for l in range(L)], dtype=torch.int64)
         self.layers = tab.to(dev)
         self.ws_bytes = int(lib().tsb_moe_decode_workspace_bytes(C.byref(self.desc)))
         self.ws = torch.zeros(self.ws_bytes, dtype=torch.uint8, device=dev)
         K = cfg["n_used"]
         self.ids = torch.zeros((L, n_tok, K), dtype=torch.int32, device=dev) if record else None
         self.w = torch.zeros((L, n_tok, K), dtype=torch.float32, device=dev) if record else None
-        self._keep = (blobs, routers, sh_blobs)
+        self.x_rec = torch.zeros((L, n_tok, cfg["n_embd"]), dtype=torch.float32, device=dev) if record_x else None
+        self._keep = (blobs, routers, sh_blobs, priors)
 
     def forward(self, x, stream=None):
         rc = lib().tsb_moe_decode_layers(C.byref(self.desc), _ptr(self.layers), _ptr(x), _ptr(self.ids), _ptr(self.w),
-                                         _ptr(self.ws), self.ws_bytes, _stream(stream))
+                                         _ptr(self.x_rec), _ptr(self.ws), self.ws_bytes, _stream(stream))
         if rc != 0:
             raise TsbError(f"moe_decode_layers: status {rc}: {lib().tsb_decode_last_error().decode()}")
         return x

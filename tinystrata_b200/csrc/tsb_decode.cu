@@ -12,6 +12,7 @@ namespace tsb {
 namespace {
 thread_local char g_derr[512];
 unsigned long long* g_trace = nullptr;
+int g_withhold = 0;
 int dfail(int code, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -83,6 +84,11 @@ int decode_check(const tsb_decode_desc* d, DecParams& p, size_t& smem) {
     return TSB_OK;
 }
 
+// This translation unit's copy of the wait bound (tsb_set_wait_limit_ns sets every copy on the current device).
+int decode_set_wait_limit(unsigned long long ns) {
+    return cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof ns) == cudaSuccess ? TSB_OK : TSB_ERR_CUDA;
+}
+
 }  // namespace tsb
 
 using namespace tsb;
@@ -95,7 +101,8 @@ uint64_t tsb_moe_decode_workspace_bytes(const tsb_decode_desc* d) {
 }
 
 int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* layers, float* x, int32_t* ids_rec,
-                          float* w_rec, void* workspace, uint64_t ws_bytes, void* stream) {
+                          float* w_rec, float* x_rec, void* workspace, uint64_t ws_bytes, void* stream) {
+    static_assert(sizeof(tsb_decode_layer) == sizeof(DecLayer), "tsb_decode_layer mirrors DecLayer");
     DecParams p{};
     size_t smem = 0;
     int rc = decode_check(d, p, smem);
@@ -126,7 +133,9 @@ int tsb_moe_decode_layers(const tsb_decode_desc* d, const tsb_decode_layer* laye
     p.err = (unsigned*) (ws + w.err);
     p.ids_rec = ids_rec;
     p.w_rec = w_rec;
+    p.x_rec = x_rec;
     p.trace = g_trace;
+    p.dbg_withhold = g_withhold;
     p.eps = d->eps;
     cudaStream_t s = (cudaStream_t) stream;
     auto kern = k_decode_layers<8>;
@@ -152,6 +161,12 @@ const char* tsb_decode_last_error(void) { return g_derr; }
 
 int tsb_moe_decode_set_trace(unsigned long long* buf) {
     g_trace = buf;
+    return TSB_OK;
+}
+
+int tsb_moe_decode_set_debug(int withhold_cta) {
+    if (withhold_cta < 0) return dfail(TSB_ERR_ARG, "decode_set_debug: a CTA index + 1, or 0");
+    g_withhold = withhold_cta;
     return TSB_OK;
 }
 

@@ -43,6 +43,7 @@ struct DecLayer {
     const uint8_t* blobs;    // [E][blob_bytes]
     const float* router;     // [E + 1][H]: the expert rows, then the shared-gate row
     const uint8_t* sh_blob;  // the shared expert
+    const float* prior;      // optional [T][E] added to the router logits before the softmax (null: none)
 };
 
 struct DecParams {
@@ -62,8 +63,10 @@ struct DecParams {
     uint64_t* xt;             // [T][H] the residual stream after each layer
     int32_t* ids_rec;         // [layers][T][K] or null
     float* w_rec;
+    float* x_rec;             // [layers][T][H]: x after each layer, or null
     unsigned* err;
     unsigned long long* trace;   // optional phase stamps: [layer][kTraceEvents][CTA] of %globaltimer, or null
+    int dbg_withhold;         // tests of the bounded waits: CTA dbg_withhold - 1 never publishes its layer-0 logits
     float eps;
     uint32_t smem_base;       // the shared-window address the dynamic shared memory starts at (checked)
 };
@@ -156,7 +159,7 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 // microseconds, and a pass is an L2 round trip already), or give up after the bound or when another CTA has recorded
 // an error (then this CTA winds down too).  Returns true when the caller must stop waiting.
 __device__ __forceinline__ bool poll_give_up(const DecParams& p, DecShared& S, uint64_t t0, unsigned site) {
-    if (S.abort || *(volatile unsigned*) p.err != 0u || globaltimer() - t0 > kWaitNs) {
+    if (S.abort || *(volatile unsigned*) p.err != 0u || globaltimer() - t0 > wait_limit_ns()) {
         report_error(p.err, site);
         S.abort = 1;
         return true;
@@ -301,7 +304,7 @@ struct WarpStream {
         const uint64_t t0 = done ? 0 : globaltimer();
         while (!done) {
             done = mbar_try_wait(&bar[k], par);
-            if (!done && globaltimer() - t0 > kWaitNs) break;
+            if (!done && globaltimer() - t0 > wait_limit_ns()) break;
         }
         if (!__all_sync(0xffffffffu, done)) return nullptr;
         return smem_ptr + (slot[k] - smem_base);
@@ -661,7 +664,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                             }
                         }
                         acc = warp_sum(acc);
-                        if (lane == 0) st_tag(p.logits + ((size_t) t * (E + 1) + o) * 2 + half, acc, tag);
+                        const bool withheld = l == 0 && p.dbg_withhold == (int) blockIdx.x + 1;
+                        if (lane == 0 && !withheld) st_tag(p.logits + ((size_t) t * (E + 1) + o) * 2 + half, acc, tag);
                     }
                 } else {
                     const int r = u - 2 * (E + 1);
@@ -710,6 +714,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                         ld_tag2(lg + 2 * (lane + i * 32), a, b);
                         values[i] = tag_val(a) + tag_val(b);
                         ok &= tag_is(a, tag) & tag_is(b, tag);
+                    }
+                    if (L.prior) {
+#pragma unroll
+                        for (int i = 0; i < V; ++i) values[i] += __ldg(L.prior + (size_t) t * E + lane + i * 32);
                     }
                     if (lane == 0) {
                         uint64_t a, b;
@@ -949,6 +957,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 acc += S.gs[t] * tag_val(w);
                 const float xn = S.xown[t][lr] + acc;
                 p.x[(size_t) t * H + row] = xn;
+                if (p.x_rec) p.x_rec[((size_t) l * T + t) * H + row] = xn;
                 st_tag(p.xt + (size_t) t * H + row, xn, tag);
             }
         }

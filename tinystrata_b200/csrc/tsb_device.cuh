@@ -188,14 +188,17 @@ __device__ __forceinline__ uint64_t globaltimer() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-constexpr uint64_t kWaitNs = 2000000000ull;   // 2 s; a bulk copy from valid memory completes in microseconds
+// The bound of every wait, per device: 2 s unless tsb_set_wait_limit_ns changed it (a bulk copy from valid memory
+// completes in microseconds).  One copy per translation unit; the host setter writes each.
+static __device__ unsigned long long g_wait_ns = 2000000000ull;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return g_wait_ns; }
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err, unsigned site) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
+    const uint64_t t0 = globaltimer(), lim = wait_limit_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 0 && globaltimer() - t0 > kWaitNs) {
+        if ((i & 255u) == 0 && globaltimer() - t0 > lim) {
             report_error(err, site);
             return false;
         }

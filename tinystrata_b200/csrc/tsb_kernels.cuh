@@ -100,6 +100,18 @@ struct GroupArgs {
     const int32_t* n_groups;
     const int32_t* ent_dst;
     const int32_t* ent_tok;
+    int cap_groups, cap_entries;   // the caller's capacities: device counts beyond them are clamped (and reported)
+    // The group count as read on the device, at most cap_groups; a larger count is recorded at `site` in err.
+    __device__ int groups(unsigned* err, unsigned site) const {
+        const int ng = *n_groups;
+        if (ng > cap_groups && threadIdx.x == 0 && blockIdx.x == 0) report_error(err, site);
+        return ng < 0 ? 0 : (ng > cap_groups ? cap_groups : ng);
+    }
+    // Entries [e0, e1) of group g, inside [0, cap_entries).
+    __device__ void entries(int g, int& e0, int& e1) const {
+        e0 = max(grp_start[g], 0);
+        e1 = min(grp_start[g + 1], cap_entries);
+    }
 };
 
 enum : int { ACT_SWIGLU = 0, ACT_GELU_TANH = 1, ACT_SWIGLU_CLAMP = 2 };
@@ -191,7 +203,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
     WarpRing ring;
     ring.init(stages + (size_t) warp * nst * stage_bytes, bars + warp * kMaxStages, stage_bytes, nst, lane);
 
-    const int ng = *p.g.n_groups;
+    const int ng = p.g.groups(p.err, 0x110u);
     const long long n_tasks = (long long) ng * p.n_ff;
     const long long W = (long long) gridDim.x * kWarps, wg = (long long) blockIdx.x * kWarps + warp;
     const long long lo = n_tasks * wg / W, hi = n_tasks * (wg + 1) / W;
@@ -217,7 +229,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_gu(GuParams p) {
     for (long long i = lo; i < hi; ++i) {
         const int s = (int) ((i - lo) % nst);
         const int g = (int) (i / p.n_ff), r = (int) (i % p.n_ff);
-        const int e0 = p.g.grp_start[g], e1 = p.g.grp_start[g + 1];
+        int e0, e1;
+        p.g.entries(g, e0, e1);
         if (!ring.wait(s, p.err, 0x100u)) return;
         const uint8_t* gate = ring.stage(s);
         const uint8_t* up = gate + p.gu_row;
@@ -280,7 +293,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_down(DownParams p) {
     WarpRing ring;
     ring.init(stages + (size_t) warp * nst * stage_bytes, bars + warp * kMaxStages, stage_bytes, nst, lane);
 
-    const int ng = *p.g.n_groups;
+    const int ng = p.g.groups(p.err, 0x210u);
     const int chunks = p.n_embd / p.R;
     const long long n_tasks = (long long) ng * chunks;
     const long long W = (long long) gridDim.x * kWarps, wg = (long long) blockIdx.x * kWarps + warp;
@@ -303,7 +316,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_expert_down(DownParams p) {
     for (long long i = lo; i < hi; ++i) {
         const int s = (int) ((i - lo) % nst);
         const int g = (int) (i / chunks), r0 = (int) (i % chunks) * p.R;
-        const int e0 = p.g.grp_start[g], e1 = p.g.grp_start[g + 1];
+        int e0, e1;
+        p.g.entries(g, e0, e1);
         if (!ring.wait(s, p.err, 0x200u)) return;
         const uint8_t* rows = ring.stage(s);
         for (int eb = e0; eb < e1; eb += NC) {

@@ -15,6 +15,8 @@
 
 namespace tsb {
 
+int decode_set_wait_limit(unsigned long long ns);   // tsb_decode.cu: that translation unit's copy of the bound
+
 // ================================================================================================ host error state
 static thread_local char g_err[512] = "";
 
@@ -33,24 +35,47 @@ static int cuda_status(const char* what) {
 static inline cudaStream_t cs(void* s) { return (cudaStream_t) s; }
 static bool aligned(const void* p, size_t a) { return ((uintptr_t) p % a) == 0; }
 
+// The device error word (a bounded wait that gave up records its site): one module global per device, zero when the
+// module loads; tsb_device_error reads and clears it.
+static __device__ unsigned g_dev_err;
+
 struct DevInfo {
     int sms = 0;
-    unsigned* err = nullptr;   // device error word (bounded waits that gave up)
+    unsigned* err = nullptr;        // the device address of g_dev_err
+    unsigned long long attr = 0;    // kernels whose large shared-memory opt-in is set on this device (bit per kernel)
 };
 static DevInfo g_dev[64];
 static std::mutex g_dev_mu;
 
+// The current device's entry, set up on its first use (the SM count and the error word's address; the lookup may load
+// the module, so a process makes its first call on a device outside any stream capture).
 static DevInfo* dev_info() {
     int d = 0;
     if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= 64) return nullptr;
     std::lock_guard<std::mutex> lk(g_dev_mu);
     DevInfo& I = g_dev[d];
     if (I.sms == 0) {
-        cudaDeviceGetAttribute(&I.sms, cudaDevAttrMultiProcessorCount, d);
-        if (cudaMalloc(&I.err, sizeof(unsigned)) != cudaSuccess) return nullptr;
-        cudaMemset(I.err, 0, sizeof(unsigned));
+        void* ep = nullptr;
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) != cudaSuccess ||
+            cudaGetSymbolAddress(&ep, g_dev_err) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        I.err = (unsigned*) ep;
+        I.sms = sms;
     }
     return &I;
+}
+// Opt kernel `bit` of this device into `bytes` of dynamic shared memory once (the attribute is per device).
+template <typename K>
+static int smem_optin(DevInfo* di, int bit, K kern, size_t bytes, const char* what) {
+    if (di->attr >> bit & 1ull) return TSB_OK;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) bytes) != cudaSuccess)
+        return cuda_status(what);
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    di->attr |= 1ull << bit;
+    return TSB_OK;
 }
 
 // ================================================================================================ formats (host)
@@ -546,8 +571,16 @@ int tsb_device_error(unsigned* code, int clear) {
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
     unsigned v = 0;
     if (cudaMemcpy(&v, di->err, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return cuda_status("device error");
-    if (clear) cudaMemset(di->err, 0, sizeof(unsigned));
+    if (clear && cudaMemset(di->err, 0, sizeof(unsigned)) != cudaSuccess) return cuda_status("device error: clear");
     if (code) *code = v;
+    return TSB_OK;
+}
+
+int tsb_set_wait_limit_ns(uint64_t ns) {
+    if (ns < 100000ull || ns > 60000000000ull) return fail(TSB_ERR_ARG, "set_wait_limit_ns: 1e5 .. 6e10 ns");
+    const unsigned long long v = ns;
+    if (cudaMemcpyToSymbol(g_wait_ns, &v, sizeof v) != cudaSuccess) return cuda_status("set_wait_limit_ns");
+    if (decode_set_wait_limit(v) != TSB_OK) return cuda_status("set_wait_limit_ns (decode)");
     return TSB_OK;
 }
 
@@ -716,7 +749,8 @@ int tsb_native_expert_grouped(const tsb_expert_layout* L, const uint64_t* grp_pt
         return fail(TSB_ERR_ALIGN, "native_expert_grouped: blob offsets must be multiples of 16 bytes");
     DevInfo* di = dev_info();
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
-    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok,
+                      (int) std::min<int64_t>(cap_groups, INT32_MAX), (int) std::min<int64_t>(cap_entries, INT32_MAX)};
     float* h = (float*) scratch;
     if (g_phase != 2) {
         const int rc = gu_dispatch(L, g, cap_groups, x_q8_1, h, ACT_SWIGLU, INFINITY, cs(stream), di);
@@ -738,7 +772,8 @@ int tsb_native_expert_grouped_act(const tsb_expert_layout* L, const uint64_t* gr
         return fail(TSB_ERR_UNSUPPORTED, "native_expert_grouped_act: unsupported layout");
     DevInfo* di = dev_info();
     if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
-    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok,
+                      (int) std::min<int64_t>(cap_groups, INT32_MAX), (int) std::min<int64_t>(cap_entries, INT32_MAX)};
     float* h = (float*) scratch;
     if (g_phase != 2) {
         const int rc = gu_dispatch(L, g, cap_groups, x_q8_1, h, act, limit, cs(stream), di);
@@ -799,24 +834,17 @@ int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t
 template <int MODE, bool A16, bool W16>
 static int pf_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
     auto kern = k_pf_gemm<MODE, A16, W16>;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPfSmem) != cudaSuccess)
-            return cuda_status("prefill: shared memory");
-        attr = true;
-    }
+    const int rc = smem_optin(di, MODE * 4 + A16 * 2 + W16, kern, kPfSmem, "prefill: shared memory");
+    if (rc != TSB_OK) return rc;
     kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
     return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
 }
 template <int MODE, int WT, bool A16>
 static int pfx_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
     auto kern = k_pf_gemm_x<MODE, WT, A16>;
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kPxSmem) != cudaSuccess)
-            return cuda_status("prefill: shared memory");
-        attr = true;
-    }
+    const int wi = WT == T_Q4_K ? 0 : WT == T_Q6_K ? 1 : WT == T_IQ3_XXS ? 2 : WT == T_Q8_0 ? 3 : 4;
+    const int rc = smem_optin(di, 8 + (wi * 2 + MODE) * 2 + A16, kern, kPxSmem, "prefill: shared memory");
+    if (rc != TSB_OK) return rc;
     kern<<<di->sms, kPfThreads, kPxSmem, s>>>(pp);
     return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
 }
@@ -923,19 +951,17 @@ int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t
 
 // ------------------------------------------------------------------------------------ no-allocation grouped experts
 // tsb_native_expert_grouped with its scratch (the entries' hidden vectors, fp32 [cap_entries][n_ff]) in a fixed
-// device array of this library instead of a caller buffer, and a bounded-wait error word of its own.  Both are
-// zero-initialised when the module loads; the hidden vectors need no clearing (the gate/up kernel writes every entry
-// the down kernel then reads), and the error word is only ever set (a wait that gave up), never cleared here.
+// device array of this library instead of a caller buffer.  The array is zero when the module loads and needs no
+// clearing between calls (the gate/up kernel writes every entry the down kernel then reads).  A bounded wait that gives
+// up records its site in the device error word every entry point shares (tsb_device_error).  The cached addresses
+// belong to the module instance of the device's current context: they do not survive a cudaDeviceReset.
 // One copy per device: two calls in flight at the same time on one device (other streams, other threads) race on it.
 static constexpr size_t kNoAllocScratchBytes = (size_t) 1 << 20;   // 1 MiB: 128 entries x n_ff 2048 fp32
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
-static __device__ __align__(256) unsigned g_noalloc_err;
 
 struct NoAllocDev {
     bool ready = false;
-    int sms = 0;
     void* scratch = nullptr;
-    unsigned* err = nullptr;
 };
 static NoAllocDev g_noalloc[64];
 static std::mutex g_noalloc_mu;
@@ -951,17 +977,13 @@ static int noalloc_dev(NoAllocDev*& out) {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     NoAllocDev& N = g_noalloc[d];
     if (!N.ready) {
-        cudaError_t e = cudaDeviceGetAttribute(&N.sms, cudaDevAttrMultiProcessorCount, d);
         void* sp = nullptr;
-        void* ep = nullptr;
-        if (e == cudaSuccess) e = cudaGetSymbolAddress(&sp, g_noalloc_scratch);
-        if (e == cudaSuccess) e = cudaGetSymbolAddress(&ep, g_noalloc_err);
+        const cudaError_t e = cudaGetSymbolAddress(&sp, g_noalloc_scratch);
         if (e != cudaSuccess) {
             cudaGetLastError();
             return fail(TSB_ERR_CUDA, "native_expert_grouped_noalloc: device %d: %s", d, cudaGetErrorString(e));
         }
         N.scratch = sp;
-        N.err = (unsigned*) ep;
         N.ready = true;
     }
     out = &N;
@@ -989,14 +1011,14 @@ int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t
     NoAllocDev* N = nullptr;
     const int rc = noalloc_dev(N);
     if (rc != TSB_OK) return rc;
-    DevInfo di;
-    di.sms = N->sms;
-    di.err = N->err;
-    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok};
+    DevInfo* di = dev_info();   // the SM count and the device error word tsb_device_error reads
+    if (!di) return fail(TSB_ERR_CUDA, "native_expert_grouped_noalloc: no CUDA device");
+    const GroupArgs g{(const unsigned long long*) grp_ptr, grp_start, n_groups, ent_dst, ent_tok,
+                      (int) std::min<int64_t>(cap_groups, INT32_MAX), (int) std::min<int64_t>(cap_entries, INT32_MAX)};
     float* h = (float*) N->scratch;
-    const int r1 = gu_dispatch(L, g, cap_groups, x_q8_1, h, ACT_SWIGLU, INFINITY, cs(stream), &di);
+    const int r1 = gu_dispatch(L, g, cap_groups, x_q8_1, h, ACT_SWIGLU, INFINITY, cs(stream), di);
     if (r1 != TSB_OK) return r1;
-    return down_dispatch(L, g, cap_groups, h, out, cs(stream), &di);
+    return down_dispatch(L, g, cap_groups, h, out, cs(stream), di);
 }
 
 int tsb_debug_row_calls(int ggml_type, const void* row, const void* x_q8_1, int64_t n, int32_t* sumi, float* val,

@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm_x(PfParams p) {
                     const uint32_t par = ((it / kPxStages) - 1) & 1u;
                     const uint64_t t0 = globaltimer();
                     while (!mbar_try_wait(&empty[s], par))
-                        if (globaltimer() - t0 > kWaitNs || abort_flag) {
+                        if (globaltimer() - t0 > wait_limit_ns() || abort_flag) {
                             report_error(p.err, 0x511u);
                             abort_flag = 1;
                             return false;

@@ -29,6 +29,8 @@ class EPPlan:
 
     def __init__(self, ids: torch.Tensor, w: torch.Tensor, n_expert: int, world: int, cyclic: bool = False):
         T, K = ids.shape
+        if n_expert % world:
+            raise ValueError(f"expert parallelism: {n_expert} experts do not split evenly over {world} ranks")
         per = n_expert // world
         if cyclic:
             dest = torch.remainder(ids.long(), world)                                   # [T, K]

@@ -58,14 +58,18 @@ class MoELayer:
             self._sh_T = T
 
     def forward(self, x: torch.Tensor, h: torch.Tensor, hq: torch.Tensor, h_next: torch.Tensor | None = None,
-                hq_next: torch.Tensor | None = None, eps: float = 1e-6, stream=None):
+                hq_next: torch.Tensor | None = None, eps: float = 1e-6, stream=None, prior: torch.Tensor | None = None):
         """x += MoE(h) for T = x.shape[0] tokens; h (fp32) feeds the router, hq (q8_1) the experts.  With h_next /
-        hq_next the next layer's RMS-normed input and its q8_1 image are written too."""
+        hq_next the next layer's RMS-normed input and its q8_1 image are written too.  prior (optional, [T, E]) is
+        added to the router logits before the softmax, as the fused decode path's logit_prior."""
         cfg = self.cfg
         T = x.shape[0]
         K, E = self.K, self.E
         logits = self.logits[:T]
         router_logits_f32(self.router, h, logits, ld=self.rows, stream=stream)
+        if prior is not None:
+            with torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream()):
+                logits[:, :E].add_(prior)
         mode = cfg["router_mode"]
         if mode == "softmax":
             native_router_topk(logits, K, E, self.ids[:T], self.w[:T], stream=stream)
@@ -103,7 +107,8 @@ class MoELayer:
 class PrefillLayer:
     """One MoE layer's prompt path for up to max_tokens tokens on the tensor cores (the reference's call stack C, the
     prompt branch: router, routing, permutation, MMQ gate/up + activation, MMQ down, shared expert, moe_sum;
-    src/gemma4/engine.cpp:2436-2457 with src/prefill/moe_mmq.cu:334-384).  Weights as MoELayer's; Q4_0 experts."""
+    src/gemma4/engine.cpp:2436-2457 with src/prefill/moe_mmq.cu:334-384).  Weights as MoELayer's, in any format the
+    tensor-core path takes (Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)."""
 
     def __init__(self, cfg: dict, blobs, router, sh_blob=None, max_tokens: int = 8192, escale=None, bias=None):
         import torch
