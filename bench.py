@@ -327,7 +327,7 @@ def bench_ep_qwen(args):
         ids, w = TS.native_router_topk(lg.contiguous(), K)       # softmax top-8, renormalised (the Qwen router)
         xq = TS.quantize_q8_1_rows(x0)
         out = ep_forward(xq, ids, w, E, H, fn, cyclic=True)
-        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xq, None, cfg["act"])
+        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, TS.mmq_quantize(x0), cfg["act"])
         shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
         return out.addcmul_(shared, torch.sigmoid(logits[:, E:E + 1]))
 
@@ -408,7 +408,7 @@ def bench_ep(args):
         ids, w = TS.route_rows(logits, K, 0, cfg["in_scale"], None, escale, True, 0.0)
         xq = TS.quantize_q8_1_rows(x0)
         out = ep_forward(xq, ids, w, E, H, fn)
-        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xq, None, cfg["act"])
+        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, TS.mmq_quantize(x0), cfg["act"])
         shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
         return out.add_(shared)
 

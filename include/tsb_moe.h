@@ -133,20 +133,33 @@ int tsb_native_expert_grouped_noalloc(const tsb_expert_layout* L, const uint64_t
                                       int64_t cap_groups, int64_t cap_entries, const void* x_q8_1, float* out,
                                       void* stream);
 
-/* Prefill grouped gate/up on the tensor cores: for group g (rows [bounds[g], bounds[g+1]), weights blobs + g *
- * blob_stride in layout L; bounds null: one group of n_rows rows), h[row] = q8_1(act(gate . x, up . x)) with x the
- * q8_1 row row_tok ? row_tok[row] : row of x_q8_1 (n_embd / 32 blocks per row, as quantize_q8_1_rows writes it);
- * h_q8_1 holds n_rows x n_ff / 32 blocks.  The block dots are exact and scaled and summed in fp32 block after block,
- * as the reference's.  act as tsb_native_expert_grouped_act.  Weights Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS or IQ3_S
- * (L's gu_type); n_embd and n_ff multiples of 64, at least 128, and of 256 for the K-quant and i-quant formats.  Replaces the gate/up mmq::Context::run + mmq::swiglu + the re-quantisation of
- * the prompt path (src/prefill/moe_mmq.cu:334-384, 123-131). */
+/* --------------------------------------------------------------------------------------------- prefill (prompt path)
+ * The activations of the tensor-core products live in the "mmq" layout, the role of the reference's block_q8_1_mmq
+ * (include/strata/prefill/moe_mmq.hpp:37): int8 codes [rows][K], then fp32 block scales d [rows][ldS] (the q8_1 fp16
+ * scale, as a float) and d * (sum of the block's codes) [rows][ldS], ldS = K / 32 rounded up to a multiple of 4, each
+ * part starting on 256 bytes.  Codes and scales are the q8_1 quantiser's, bit for bit.  Buffers 256-byte aligned. */
+uint64_t tsb_mmq_act_bytes(int64_t rows, int64_t K);
+/* fp32 rows -> mmq layout: output row r quantises row row_src[r] of x (null: row r; row stride ld_x floats).  The gather
+ * puts the entries in expert order for the grouped products.  Replaces mmq::quantize(x, ids, xq, ...) (moe_mmq.hpp:37,
+ * src/prefill/moe_mmq.cu:322) and Mmq::quantize (src/gemma4/mmq.hpp:31-41). */
+int tsb_mmq_quantize(const float* x, int64_t ld_x, const int32_t* row_src, int n_rows, int K, void* act, void* stream);
+/* q8_1 blocks (quantize_q8_1_rows's) -> mmq layout, output row r from row row_src[r] (null: r); the same codes and scales.
+ * For activations that arrive already quantised (an expert-parallel exchange). */
+int tsb_mmq_from_q8_1(const void* x_q8_1, const int32_t* row_src, int n_rows, int K, void* act, void* stream);
+/* Prefill grouped gate/up on the tensor cores (tcgen05.mma.kind::i8, TMA-loaded activation tiles): for group g (rows
+ * [bounds[g], bounds[g+1]) of x_act, weights blobs + g * blob_stride in layout L; bounds null: one group of n_rows rows),
+ * h[row] = q8_1(act(gate . x, up . x)) written to h_act in the mmq layout (tsb_mmq_act_bytes(n_rows, n_ff)).  Per
+ * 32-value block the integer dot is exact (int32 in tensor memory) and is scaled and summed in fp32 block after block,
+ * as the reference's.  act as tsb_native_expert_grouped_act.  Weights Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS or IQ3_S (L's
+ * gu_type); n_embd a multiple of 64 (>= 128) and of 256 for the K-quant and i-quant formats, n_ff a multiple of 64;
+ * at most 512 groups.  Replaces the gate/up mmq::Context::run + mmq::swiglu + the re-quantisation of the prompt path
+ * (include/strata/prefill/moe_mmq.hpp:58-81, src/prefill/moe_mmq.cu:334-384, 123-131; src/gemma4/mmq.cu:74-110). */
 int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
-                       int n_groups, int n_rows, const void* x_q8_1, const int32_t* row_tok, void* h_q8_1, int act,
-                       float limit, void* stream);
-/* Prefill grouped down: out[row] = down . h[row] (fp32 [n_rows][n_embd], 16-byte aligned) with the groups as above
- * and h the q8_1 rows tsb_moe_prefill_gu wrote.  Replaces the down mmq::Context::run (src/prefill/moe_mmq.cu:334-384). */
+                       int n_groups, int n_rows, const void* x_act, void* h_act, int act, float limit, void* stream);
+/* Prefill grouped down: out[row] = down . h[row] (fp32 [n_rows][n_embd], 16-byte aligned) with the groups as above and
+ * h_act the hidden rows tsb_moe_prefill_gu wrote.  Replaces the down mmq::Context::run (src/prefill/moe_mmq.cu:334-384). */
 int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
-                         int n_groups, int n_rows, const void* h_q8_1, float* out, void* stream);
+                         int n_groups, int n_rows, const void* h_act, float* out, void* stream);
 
 /* Bench only: 0 = both expert kernels (default), 1 = gate/up + activation only, 2 = down only (reads the scratch the
  * previous call left).  Replaces native_expert_set_mode's phase argument (iq_kernels.hpp:85).  Process-wide; set
@@ -219,6 +232,13 @@ int tsb_moe_decode_set_debug(int withhold_cta);
  * expert kernels compute them (calls in row_dot order, src/kernels/cuda/iq_kernels.cu:695-705).  Parity tests only. */
 int tsb_debug_row_calls(int ggml_type, const void* row, const void* x_q8_1, int64_t n, int32_t* sumi, float* val,
                         void* stream);
+/* The tensor-core block sums of the prefill products: one launch of the gate/up (mode 0, output h_act) or down (mode 1,
+ * output out) kernel over one expert blob and n_rows rows of x_act, which also stores the int32 block sums of its first
+ * tile (rows 0..127, tile columns 0..127) in sums: [K / 32][split][128 rows][128 columns], split 2 for Q6_K (its 16-value
+ * halves) and 1 otherwise.  Gate/up tile columns interleave gate and up rows in 32-row groups (columns 0-31 gate rows
+ * 0-31, 32-63 up rows 0-31, 64-95 gate rows 32-63, 96-127 up rows 32-63).  Parity tests only. */
+int tsb_debug_mmq_block_sums(const tsb_expert_layout* L, int mode, const void* blob, int n_rows, const void* x_act,
+                             void* h_act, float* out, int32_t* sums, void* stream);
 
 #ifdef __cplusplus
 }

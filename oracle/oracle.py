@@ -68,6 +68,7 @@ def lib():
             L.or_row_dot.argtypes = [C.c_int, _p, _p, _i64]
             L.or_mat_vec.argtypes = [C.c_int, _p, _p, _i64, _i64, _p]
             L.or_dequant_row.argtypes = [C.c_int, _p, _i64, _p]
+            L.or_weight_codes.argtypes = [C.c_int, _p, _i64, _p]
             L.or_router_softmax_topk.restype = C.c_int
             L.or_router_softmax_topk.argtypes = [_p, C.c_int, C.c_int, C.c_int, C.c_int, _p, _p, _f]
             L.or_route_rows.argtypes = [_p, C.c_int, C.c_int, C.c_int, C.c_int, _f, _p, _p, C.c_int, _f, _p, _p]
@@ -178,6 +179,15 @@ def mat_vec(t: int, w: np.ndarray, xq: np.ndarray, n_in: int, n_out: int) -> np.
     y = np.zeros(n_out, np.float32)
     lib().or_mat_vec(t, _ptr(np.ascontiguousarray(w)), _ptr(np.ascontiguousarray(xq)), n_in, n_out, _ptr(y))
     return y
+
+
+def weight_codes(t: int, rows: np.ndarray, n: int) -> np.ndarray:
+    """int8 [rows, n]: the integer weight codes the block dots multiply the activation codes by (or_weight_codes)."""
+    rows = np.ascontiguousarray(rows, dtype=np.uint8).reshape(-1, row_bytes(t, n))
+    out = np.empty((rows.shape[0], n), dtype=np.int8)
+    for r in range(rows.shape[0]):
+        lib().or_weight_codes(t, _ptr(rows[r]), n, _ptr(out[r]))
+    return out
 
 
 def dequant_row(t: int, row: np.ndarray, n: int) -> np.ndarray:

@@ -458,6 +458,81 @@ void or_dequant_row(int type, const uint8_t* row, int64_t n, float* out) {
     }
 }
 
+/* The integer weight codes each block dot multiplies the q8_1 codes by, per value of a row of n values: Q4_0 nibble - 8
+ * (q4_0_centred), Q8_0 the int8 code, Q4_K the nibble (its min is a separate term), Q6_K the 6-bit code - 32, IQ3_XXS /
+ * IQ3_S the grid byte with its sign applied (the dp4a operands of iq_kernels.cu:188-236, 314-386, 457-474, 523-566).
+ * The layouts are the ones or_dequant_row decodes; a tensor-core block sum is the plain integer dot of these codes with
+ * the activation codes over the block's values. */
+void or_weight_codes(int type, const uint8_t* row, int64_t n, int8_t* out) {
+    const int qk = or_block_values(type), bb = or_block_bytes(type);
+    for (int64_t b = 0; b < n / qk; ++b) {
+        const uint8_t* w = row + b * bb;
+        int8_t* y = out + b * qk;
+        switch (type) {
+            case T_IQ3_XXS:
+                for (int s = 0; s < 8; ++s) {
+                    const uint32_t aux = u32_at(w + 2 + 64 + 4 * s);
+                    for (int l = 0; l < 4; ++l) {
+                        const uint8_t s8 = k_ksigns[(aux >> (7 * l)) & 127];
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t g = k_iq3xxs_grid[w[2 + 8 * s + 2 * l + h]];
+                            for (int j = 0; j < 4; ++j) {
+                                const int v = (int) ((g >> (8 * j)) & 0xff);
+                                y[32 * s + 8 * l + 4 * h + j] = (int8_t) (((s8 >> (4 * h + j)) & 1) ? -v : v);
+                            }
+                        }
+                    }
+                }
+                break;
+            case T_IQ3_S:
+                for (int s = 0; s < 8; ++s) {
+                    const uint8_t qh = w[66 + s];
+                    for (int l = 0; l < 4; ++l) {
+                        const uint8_t s8 = w[74 + 4 * s + l];
+                        for (int h = 0; h < 2; ++h) {
+                            const int j8 = 2 * l + h;
+                            const uint32_t g = k_iq3s_grid[w[2 + 8 * s + j8] | (((qh >> j8) & 1) << 8)];
+                            for (int j = 0; j < 4; ++j) {
+                                const int v = (int) ((g >> (8 * j)) & 0xff);
+                                y[32 * s + 8 * l + 4 * h + j] = (int8_t) (((s8 >> (4 * h + j)) & 1) ? -v : v);
+                            }
+                        }
+                    }
+                }
+                break;
+            case T_Q4_0:
+                for (int j = 0; j < 16; ++j) {
+                    y[j] = (int8_t) ((w[2 + j] & 15) - 8);
+                    y[j + 16] = (int8_t) ((w[2 + j] >> 4) - 8);
+                }
+                break;
+            case T_Q8_0:
+                for (int j = 0; j < 32; ++j) y[j] = (int8_t) w[2 + j];
+                break;
+            case T_Q4_K:
+                for (int j = 0; j < 4; ++j)
+                    for (int l = 0; l < 32; ++l) {
+                        y[64 * j + l] = (int8_t) (w[16 + 32 * j + l] & 15);
+                        y[64 * j + 32 + l] = (int8_t) (w[16 + 32 * j + l] >> 4);
+                    }
+                break;
+            case T_Q6_K: {
+                const uint8_t* ql = w;
+                const uint8_t* qh = w + 128;
+                for (int half = 0; half < 2; ++half)
+                    for (int l = 0; l < 32; ++l) {
+                        y[128 * half + l + 0] = (int8_t) ((int) ((ql[64 * half + l] & 0xF) | (((qh[32 * half + l] >> 0) & 3) << 4)) - 32);
+                        y[128 * half + l + 32] = (int8_t) ((int) ((ql[64 * half + l + 32] & 0xF) | (((qh[32 * half + l] >> 2) & 3) << 4)) - 32);
+                        y[128 * half + l + 64] = (int8_t) ((int) ((ql[64 * half + l] >> 4) | (((qh[32 * half + l] >> 4) & 3) << 4)) - 32);
+                        y[128 * half + l + 96] = (int8_t) ((int) ((ql[64 * half + l + 32] >> 4) | (((qh[32 * half + l] >> 6) & 3) << 4)) - 32);
+                    }
+                break;
+            }
+            default: break;
+        }
+    }
+}
+
 /* ------------------------------------------------------------------------------------------------ routers */
 /* Qwen: softmax over n_expert logits (max-shifted), NaN -> -FLT_MAX, k argmax picks (lowest id on ties),
  * w = p / max(sum of picked p, 6.103515625e-5).  native_router.cu:44-95.  Returns the number of tokens whose

@@ -66,9 +66,13 @@ SIGNATURES = {
     "tsb_native_expert_grouped_act": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
                                                 C.c_int, _f, _p]),
     "tsb_moe_dispatch": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, _p, _p, _p, _p, _p]),
-    "tsb_moe_prefill_gu": (C.c_int, [C.POINTER(ExpertLayout), _p, _u64, _p, C.c_int, C.c_int, _p, _p, _p, C.c_int, _f,
+    "tsb_mmq_act_bytes": (_u64, [_i64, _i64]),
+    "tsb_mmq_quantize": (C.c_int, [_p, _i64, _p, C.c_int, C.c_int, _p, _p]),
+    "tsb_mmq_from_q8_1": (C.c_int, [_p, _p, C.c_int, C.c_int, _p, _p]),
+    "tsb_moe_prefill_gu": (C.c_int, [C.POINTER(ExpertLayout), _p, _u64, _p, C.c_int, C.c_int, _p, _p, C.c_int, _f,
                                      _p]),
     "tsb_moe_prefill_down": (C.c_int, [C.POINTER(ExpertLayout), _p, _u64, _p, C.c_int, C.c_int, _p, _p, _p]),
+    "tsb_debug_mmq_block_sums": (C.c_int, [C.POINTER(ExpertLayout), C.c_int, _p, C.c_int, _p, _p, _p, _p, _p]),
     "tsb_native_expert_grouped_noalloc": (C.c_int, [C.POINTER(ExpertLayout), _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                                                     _p]),
     "tsb_moe_combine": (C.c_int, [_p, _p, _p, _p, C.c_int, _p, _p, C.c_int, _p, _p, _p, C.c_int, _f, C.c_int, _p]),
@@ -254,28 +258,102 @@ def moe_dispatch(ids, n_expert: int, stream=None):
     return bounds, row_ent, row_tok, rinv
 
 
-def moe_prefill_gu(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, x_q8_1, row_tok=None,
-                   act: int = ACT_SWIGLU, limit: float = float("inf"), h=None, stream=None):
-    """Grouped gate/up + activation on the tensor cores: x_q8_1 (quantize_q8_1_rows's blocks) -> the hidden vectors'
-    q8_1 blocks uint8 [n_rows, n_ff / 32 * 36]."""
-    import torch
-    if h is None:
-        h = torch.empty((n_rows, L.n_ff // 32 * Q8_1_BYTES), dtype=torch.uint8, device=x_q8_1.device)
+class MmqAct:
+    """Activations in the tensor-core ("mmq") layout for `rows` rows of K values: one 256-byte aligned device buffer of
+    tsb_mmq_act_bytes(rows, K) bytes holding int8 codes [rows][K], fp32 d [rows][ldS] and d * sum(codes) [rows][ldS]
+    (ldS = K / 32 rounded up to 4).  The role of the reference's block_q8_1_mmq (moe_mmq.hpp:37)."""
+
+    def __init__(self, rows: int, K: int, device, buf=None):
+        import torch
+        self.rows, self.K = rows, K
+        self.ldS = (K // 32 + 3) // 4 * 4
+        nbytes = int(lib().tsb_mmq_act_bytes(rows, K))
+        if buf is None:
+            buf = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        assert buf.numel() >= nbytes
+        off = (-buf.data_ptr()) % 256
+        self._store = buf
+        self.buf = buf[off:off + max(nbytes, 1)]
+
+    def data_ptr(self):
+        return self.buf.data_ptr()
+
+    @property
+    def codes(self):
+        import torch
+        return self.buf[:self.rows * self.K].view(torch.int8).view(self.rows, self.K)
+
+    def _al(self, v):
+        return (v + 255) // 256 * 256
+
+    @property
+    def d(self):
+        import torch
+        o = self._al(self.rows * self.K)
+        return self.buf[o:o + self.rows * self.ldS * 4].view(torch.float32).view(self.rows, self.ldS)
+
+    @property
+    def s(self):
+        import torch
+        o = self._al(self.rows * self.K) + self._al(self.rows * self.ldS * 4)
+        return self.buf[o:o + self.rows * self.ldS * 4].view(torch.float32).view(self.rows, self.ldS)
+
+
+def mmq_quantize(x, row_src=None, n_rows: int | None = None, out: MmqAct | None = None, stream=None) -> MmqAct:
+    """fp32 rows -> mmq layout; output row r from x[row_src[r]] (tsb_mmq_quantize; the reference's mmq::quantize)."""
+    n_rows = x.shape[0] if n_rows is None else n_rows
+    K = x.shape[1]
+    out = out if out is not None else MmqAct(n_rows, K, x.device)
+    _check(lib().tsb_mmq_quantize(_ptr(x), x.stride(0), _ptr(row_src), n_rows, K, C.c_void_p(out.data_ptr()),
+                                  _stream(stream)), "mmq_quantize")
+    return out
+
+
+def mmq_from_q8_1(x_q8_1, K: int, row_src=None, n_rows: int | None = None, out: MmqAct | None = None,
+                  stream=None) -> MmqAct:
+    """q8_1 rows (uint8 [rows, K / 32 * 36]) -> mmq layout, output row r from row row_src[r]."""
+    n_rows = x_q8_1.shape[0] if n_rows is None else n_rows
+    out = out if out is not None else MmqAct(n_rows, K, x_q8_1.device)
+    _check(lib().tsb_mmq_from_q8_1(_ptr(x_q8_1), _ptr(row_src), n_rows, K, C.c_void_p(out.data_ptr()),
+                                   _stream(stream)), "mmq_from_q8_1")
+    return out
+
+
+def moe_prefill_gu(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, x_act: MmqAct,
+                   act: int = ACT_SWIGLU, limit: float = float("inf"), h: MmqAct | None = None, stream=None) -> MmqAct:
+    """Grouped gate/up + activation on the tensor cores (kind::i8): x_act rows (expert-sorted) -> the hidden vectors
+    in the mmq layout."""
+    h = h if h is not None else MmqAct(n_rows, int(L.n_ff), x_act.buf.device)
     _check(lib().tsb_moe_prefill_gu(C.byref(L), _ptr(blobs), blob_stride, _ptr(bounds), n_groups, n_rows,
-                                    _ptr(x_q8_1), _ptr(row_tok), _ptr(h), act, limit, _stream(stream)),
-           "moe_prefill_gu")
+                                    C.c_void_p(x_act.data_ptr()), C.c_void_p(h.data_ptr()), act, limit,
+                                    _stream(stream)), "moe_prefill_gu")
     return h
 
 
-def moe_prefill_down(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, h_q8_1, out=None,
-                     stream=None):
-    """Grouped down on the tensor cores: moe_prefill_gu's q8_1 rows -> fp32 [n_rows, n_embd]."""
+def moe_prefill_down(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups: int, n_rows: int, h_act: MmqAct,
+                     out=None, stream=None):
+    """Grouped down on the tensor cores: moe_prefill_gu's hidden rows -> fp32 [n_rows, n_embd]."""
     import torch
     if out is None:
-        out = torch.empty((n_rows, L.n_embd), dtype=torch.float32, device=h_q8_1.device)
+        out = torch.empty((n_rows, L.n_embd), dtype=torch.float32, device=h_act.buf.device)
     _check(lib().tsb_moe_prefill_down(C.byref(L), _ptr(blobs), blob_stride, _ptr(bounds), n_groups, n_rows,
-                                      _ptr(h_q8_1), _ptr(out), _stream(stream)), "moe_prefill_down")
+                                      C.c_void_p(h_act.data_ptr()), _ptr(out), _stream(stream)), "moe_prefill_down")
     return out
+
+
+def debug_mmq_block_sums(L: ExpertLayout, mode: int, blob, n_rows: int, x_act: MmqAct, stream=None):
+    """The int32 block sums of the first tile of one prefill launch (mode 0 gate/up, 1 down) over one expert blob:
+    [K / 32, split, 128 rows, 128 tile columns]."""
+    import torch
+    K = int(L.n_embd if mode == 0 else L.n_ff)
+    split = 2 if (L.d_type if mode == 1 else L.gu_type) == T_Q6_K else 1
+    sums = torch.zeros((K // 32, split, 128, 128), dtype=torch.int32, device=blob.device)
+    h = MmqAct(n_rows, int(L.n_ff), blob.device) if mode == 0 else None
+    out = torch.empty((n_rows, int(L.n_embd)), dtype=torch.float32, device=blob.device) if mode == 1 else None
+    _check(lib().tsb_debug_mmq_block_sums(C.byref(L), mode, _ptr(blob), n_rows, C.c_void_p(x_act.data_ptr()),
+                                          C.c_void_p(h.data_ptr()) if h is not None else None, _ptr(out), _ptr(sums),
+                                          _stream(stream)), "debug_mmq_block_sums")
+    return sums, (h if mode == 0 else out)
 
 
 def moe_combine(x, parts, wts, K, shared=None, sgate=None, sg_stride=1, prow=None, wn=None, h=None, hq=None,

@@ -3,6 +3,7 @@
 #include "tsb_kernels.cuh"
 #include "tsb_prefill.cuh"
 #include "tsb_prefill_k.cuh"
+#include "tsb_mmq.cuh"
 #include "../../include/tsb_moe.h"
 
 #include <cuda_runtime.h>
@@ -831,124 +832,223 @@ int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t
 }
 
 }  // extern "C"
-template <int MODE, bool A16, bool W16>
-static int pf_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
-    auto kern = k_pf_gemm<MODE, A16, W16>;
-    const int rc = smem_optin(di, MODE * 4 + A16 * 2 + W16, kern, kPfSmem, "prefill: shared memory");
-    if (rc != TSB_OK) return rc;
-    kern<<<di->sms, kPfThreads, kPfSmem, s>>>(pp);
-    return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
-}
-template <int MODE, int WT, bool A16>
-static int pfx_launch_t(PfParams& pp, cudaStream_t s, DevInfo* di) {
-    auto kern = k_pf_gemm_x<MODE, WT, A16>;
-    const int wi = WT == T_Q4_K ? 0 : WT == T_Q6_K ? 1 : WT == T_IQ3_XXS ? 2 : WT == T_Q8_0 ? 3 : 4;
-    const int rc = smem_optin(di, 8 + (wi * 2 + MODE) * 2 + A16, kern, kPxSmem, "prefill: shared memory");
-    if (rc != TSB_OK) return rc;
-    kern<<<di->sms, kPfThreads, kPxSmem, s>>>(pp);
-    return cuda_status(MODE == PF_GU ? "moe_prefill_gu" : "moe_prefill_down");
-}
-template <int MODE, bool A16>
-static int pfx_launch_m(int wt, PfParams& pp, cudaStream_t s, DevInfo* di) {
-    switch (wt) {
-        case T_Q4_K: return pfx_launch_t<MODE, T_Q4_K, A16>(pp, s, di);
-        case T_Q6_K: return pfx_launch_t<MODE, T_Q6_K, A16>(pp, s, di);
-        case T_IQ3_XXS: return pfx_launch_t<MODE, T_IQ3_XXS, A16>(pp, s, di);
-        case T_Q8_0: return pfx_launch_t<MODE, T_Q8_0, A16>(pp, s, di);
-        default: return pfx_launch_t<MODE, T_IQ3_S, A16>(pp, s, di);
-    }
-}
-extern "C" {
-// 16-byte windows where the rows allow them: activation rows of K / 32 q8_1 blocks (36 bytes), weight rows.
-static int pf_launch(int mode, int wt, PfParams& pp, cudaStream_t s) {
-    DevInfo* di = dev_info();
-    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
-    pp.err = di->err;
-    const bool a16 = ((pp.K / 32) * 36) % 16 == 0 && (uintptr_t) pp.X % 16 == 0;
-    if (wt != T_Q4_0) {
-        if (mode == PF_GU) return a16 ? pfx_launch_m<PF_GU, true>(wt, pp, s, di) : pfx_launch_m<PF_GU, false>(wt, pp, s, di);
-        return a16 ? pfx_launch_m<PF_DOWN, true>(wt, pp, s, di) : pfx_launch_m<PF_DOWN, false>(wt, pp, s, di);
-    }
-    const bool w16 = pp.w_row % 16 == 0 && (uintptr_t) pp.blobs % 16 == 0 && pp.blob_stride % 16 == 0 &&
-                     pp.w_off % 16 == 0 && pp.up_off % 16 == 0;
-    if (mode == PF_GU) {
-        if (a16) return w16 ? pf_launch_t<PF_GU, true, true>(pp, s, di) : pf_launch_t<PF_GU, true, false>(pp, s, di);
-        return w16 ? pf_launch_t<PF_GU, false, true>(pp, s, di) : pf_launch_t<PF_GU, false, false>(pp, s, di);
-    }
-    if (a16) return w16 ? pf_launch_t<PF_DOWN, true, true>(pp, s, di) : pf_launch_t<PF_DOWN, true, false>(pp, s, di);
-    return w16 ? pf_launch_t<PF_DOWN, false, true>(pp, s, di) : pf_launch_t<PF_DOWN, false, false>(pp, s, di);
+// ------------------------------------------------------------------------------------ prefill on the tensor cores
+// The activations' tensor-core layout (tsb_mmq_act_bytes): int8 codes [rows][K], then fp32 d [rows][ldS] and
+// d * sum(codes) [rows][ldS], ldS = K / 32 rounded up to 4 (16-byte rows for the scale tiles' TMA), each part on 256 B.
+struct MmqView {
+    int8_t* codes;
+    float* d;
+    float* s;
+    int ldS;
+};
+static int mmq_lds(int64_t K) { return (int) ((K / 32 + 3) / 4 * 4); }
+static uint64_t al256(uint64_t v) { return (v + 255) & ~255ull; }
+static MmqView mmq_view(const void* base, int64_t rows, int64_t K) {
+    MmqView v;
+    v.ldS = mmq_lds(K);
+    uint8_t* b = (uint8_t*) base;
+    v.codes = (int8_t*) b;
+    v.d = (float*) (b + al256((uint64_t) rows * K));
+    v.s = (float*) (b + al256((uint64_t) rows * K) + al256((uint64_t) rows * v.ldS * 4));
+    return v;
 }
 
-static int pf_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, int n_groups, int n_rows,
-                    int mode) {
-    if (!L || !blobs || n_rows < 0 || n_groups < 1 || n_groups > kPfMaxGroups)
-        return fail(TSB_ERR_ARG, "moe_prefill: arguments");
-    const int t = mode == PF_GU ? L->gu_type : L->d_type;
-    if (t != T_Q4_0 && t != T_Q8_0 && t != T_Q4_K && t != T_Q6_K && t != T_IQ3_XXS && t != T_IQ3_S)
-        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)", t);
-    if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 128)
-        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd and n_ff multiples of 64, at least 128");
-    const int64_t k = mode == PF_GU ? L->n_embd : L->n_ff;   // super-block formats: the contraction in 256-value blocks
-    if (t != T_Q4_0 && t != T_Q8_0 && k % 256) return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: K-quant / i-quant rows of 256-value blocks");
-    // Q4_0 rows are read in 4-byte words; the other formats' loaders take 2-byte aligned rows (Q6_K rows are 210 n / 256
-    // bytes), Q4_K's 16-byte ones (144-byte blocks)
-    const int64_t row = mode == PF_GU ? L->gu_row : L->d_row;
-    const int64_t ra = t == T_Q4_0 ? 4 : t == T_Q4_K ? 16 : 2;
-    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || row % ra)
-        return fail(TSB_ERR_ALIGN, "moe_prefill: blob alignment");
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn tmap_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn) f;
+        cudaGetLastError();
+    });
+    return fn;
+}
+// A 2-D map over [h][w] elements (row pitch `pitch` bytes) read in boxes of box_h x box_w; loads past the extent read 0.
+static int tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t w, uint64_t h, uint64_t pitch,
+                   uint32_t box_w, uint32_t box_h, CUtensorMapSwizzle sw) {
+    EncodeTiledFn enc = tmap_encoder();
+    if (!enc) return fail(TSB_ERR_CUDA, "prefill: cuTensorMapEncodeTiled is not available");
+    const cuuint64_t dims[2] = {w, h};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {box_w, box_h};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(TSB_ERR_CUDA, "prefill: tensor map (%llu x %llu, pitch %llu): error %d",
+                                       (unsigned long long) h, (unsigned long long) w, (unsigned long long) pitch, (int) r);
     return TSB_OK;
 }
 
-int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
-                       int n_groups, int n_rows, const void* x_q8_1, const int32_t* row_tok, void* h_q8_1, int act,
-                       float limit, void* stream) {
-    int rc = pf_check(L, blobs, blob_stride, n_groups, n_rows, PF_GU);
+template <int MODE, int WT>
+static int mq_launch_t(const MqParams& pp, const MmqView& xa, cudaStream_t s, DevInfo* di) {
+    using LY = MqLayout<WT>;
+    auto kern = k_mmq<MODE, WT>;
+    const int wi = WT == T_Q4_0 ? 0 : WT == T_Q8_0 ? 1 : WT == T_Q4_K ? 2 : WT == T_Q6_K ? 3 : WT == T_IQ3_XXS ? 4 : 5;
+    int rc = smem_optin(di, 32 + wi * 2 + MODE, kern, LY::kSmem, "prefill: shared memory");
     if (rc != TSB_OK) return rc;
+    CUtensorMap tx, tdx, tsx;
+    rc = tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xa.codes, (uint64_t) pp.K, (uint64_t) pp.n_rows, (uint64_t) pp.K,
+                 kMqBK, kMqBM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == TSB_OK)
+        rc = tmap_2d(&tdx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xa.d, (uint64_t) (pp.K / 32), (uint64_t) pp.n_rows,
+                     (uint64_t) xa.ldS * 4, kMqBlk, kMqBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc == TSB_OK)
+        rc = tmap_2d(&tsx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xa.s, (uint64_t) (pp.K / 32), (uint64_t) pp.n_rows,
+                     (uint64_t) xa.ldS * 4, kMqBlk, kMqBM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != TSB_OK) return rc;
+    kern<<<di->sms, kMqThreads, LY::kSmem, s>>>(tx, tdx, tsx, pp);
+    return cuda_status(MODE == MQ_GU ? "moe_prefill_gu" : "moe_prefill_down");
+}
+template <int MODE>
+static int mq_launch(int wt, const MqParams& pp, const MmqView& xa, cudaStream_t s, DevInfo* di) {
+    switch (wt) {
+        case T_Q4_0: return mq_launch_t<MODE, T_Q4_0>(pp, xa, s, di);
+        case T_Q8_0: return mq_launch_t<MODE, T_Q8_0>(pp, xa, s, di);
+        case T_Q4_K: return mq_launch_t<MODE, T_Q4_K>(pp, xa, s, di);
+        case T_Q6_K: return mq_launch_t<MODE, T_Q6_K>(pp, xa, s, di);
+        case T_IQ3_XXS: return mq_launch_t<MODE, T_IQ3_XXS>(pp, xa, s, di);
+        case T_IQ3_S: return mq_launch_t<MODE, T_IQ3_S>(pp, xa, s, di);
+        default: return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d", wt);
+    }
+}
+
+extern "C" {
+
+uint64_t tsb_mmq_act_bytes(int64_t rows, int64_t K) {
+    if (rows < 0 || K <= 0 || K % 32) return 0;
+    return al256((uint64_t) rows * K) + 2 * al256((uint64_t) rows * mmq_lds(K) * 4);
+}
+
+int tsb_mmq_quantize(const float* x, int64_t ld_x, const int32_t* row_src, int n_rows, int K, void* act, void* stream) {
     if (n_rows == 0) return TSB_OK;
-    if (!x_q8_1 || !h_q8_1 || act < 0 || act > 2 || (bounds == nullptr && n_groups != 1))
-        return fail(TSB_ERR_ARG, "moe_prefill_gu: arguments");
-    if ((uintptr_t) x_q8_1 % 4 || (uintptr_t) h_q8_1 % 4) return fail(TSB_ERR_ALIGN, "moe_prefill_gu: q8_1 alignment");
-    PfParams pp{};
+    if (!x || !act || n_rows < 0 || K <= 0 || K % 32 || ld_x < K) return fail(TSB_ERR_ARG, "mmq_quantize: arguments");
+    if ((uintptr_t) act % 256) return fail(TSB_ERR_ALIGN, "mmq_quantize: the activation buffer must be 256-byte aligned");
+    const MmqView v = mmq_view(act, n_rows, K);
+    const long long warps = (long long) n_rows * (K / 32);
+    k_mmq_quantize<<<(unsigned) ((warps + 7) / 8), 256, 0, cs(stream)>>>(x, ld_x, row_src, n_rows, K, v.codes, v.d, v.s,
+                                                                          v.ldS);
+    return cuda_status("mmq_quantize");
+}
+
+int tsb_mmq_from_q8_1(const void* x_q8_1, const int32_t* row_src, int n_rows, int K, void* act, void* stream) {
+    if (n_rows == 0) return TSB_OK;
+    if (!x_q8_1 || !act || n_rows < 0 || K <= 0 || K % 32) return fail(TSB_ERR_ARG, "mmq_from_q8_1: arguments");
+    if ((uintptr_t) act % 256 || (uintptr_t) x_q8_1 % 4) return fail(TSB_ERR_ALIGN, "mmq_from_q8_1: alignment");
+    const MmqView v = mmq_view(act, n_rows, K);
+    const long long warps = (long long) n_rows * (K / 32);
+    k_mmq_from_q8_1<<<(unsigned) ((warps + 7) / 8), 256, 0, cs(stream)>>>((const BlockQ8_1*) x_q8_1, row_src, n_rows, K,
+                                                                           v.codes, v.d, v.s, v.ldS);
+    return cuda_status("mmq_from_q8_1");
+}
+
+}  // extern "C"
+
+static int mq_check(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, int n_groups, int n_rows,
+                    int mode) {
+    if (!L || !blobs || n_rows < 0 || n_groups < 1 || n_groups > kMqMaxGroups)
+        return fail(TSB_ERR_ARG, "moe_prefill: arguments (1 .. %d groups)", kMqMaxGroups);
+    const int t = mode == MQ_GU ? L->gu_type : L->d_type;
+    if (t != T_Q4_0 && t != T_Q8_0 && t != T_Q4_K && t != T_Q6_K && t != T_IQ3_XXS && t != T_IQ3_S)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: weight type %d (Q4_0, Q8_0, Q4_K, Q6_K, IQ3_XXS, IQ3_S)", t);
+    if (L->n_embd % 64 || L->n_ff % 64 || L->n_embd < 128 || L->n_ff < 64)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: n_embd a multiple of 64 (>= 128), n_ff a multiple of 64");
+    const int64_t k = mode == MQ_GU ? L->n_embd : L->n_ff;
+    if (t != T_Q4_0 && t != T_Q8_0 && k % 256)
+        return fail(TSB_ERR_UNSUPPORTED, "moe_prefill: K-quant / i-quant rows of 256-value blocks");
+    // rows are read in aligned words: 4-byte (Q4_0, Q8_0: an even number of blocks), 16-byte (Q4_K), 2-byte (the rest)
+    const int64_t row = mode == MQ_GU ? L->gu_row : L->d_row;
+    const int64_t ra = (t == T_Q4_0 || t == T_Q8_0) ? 4 : t == T_Q4_K ? 16 : 2;
+    if ((uintptr_t) blobs % 16 || blob_stride % 16 || L->up_off % 16 || L->down_off % 16 || row % ra)
+        return fail(TSB_ERR_ALIGN, "moe_prefill: blob alignment (rows of %lld bytes)", (long long) row);
+    return TSB_OK;
+}
+
+static MqParams mq_params(const tsb_expert_layout* L, int mode, const void* blobs, uint64_t blob_stride,
+                          const int32_t* bounds, int n_groups, int n_rows) {
+    MqParams pp{};
     pp.bounds = bounds;
     pp.n_groups = n_groups;
     pp.n_rows = n_rows;
     pp.blobs = (const uint8_t*) blobs;
     pp.blob_stride = blob_stride;
-    pp.w_off = 0;
-    pp.up_off = L->up_off;
-    pp.w_row = (uint32_t) L->gu_row;
-    pp.K = (int) L->n_embd;
-    pp.N = (int) L->n_ff;
-    pp.X = (const BlockQ8_1*) x_q8_1;
-    pp.row_tok = row_tok;
-    pp.Hq = (BlockQ8_1*) h_q8_1;
+    if (mode == MQ_GU) {
+        pp.w_off = 0;
+        pp.up_off = L->up_off;
+        pp.w_row = (uint32_t) L->gu_row;
+        pp.K = (int) L->n_embd;
+        pp.N = (int) L->n_ff;
+    } else {
+        pp.w_off = L->down_off;
+        pp.w_row = (uint32_t) L->d_row;
+        pp.K = (int) L->n_ff;
+        pp.N = (int) L->n_embd;
+    }
+    pp.act = ACT_SWIGLU;
+    pp.limit = INFINITY;
+    return pp;
+}
+
+static int mq_run(const tsb_expert_layout* L, int mode, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                  int n_groups, int n_rows, const void* x_act, void* h_act, float* out, int act, float limit,
+                  int32_t* dbg, cudaStream_t s) {
+    int rc = mq_check(L, blobs, blob_stride, n_groups, n_rows, mode);
+    if (rc != TSB_OK) return rc;
+    if (n_rows == 0) return TSB_OK;
+    if (!x_act || (mode == MQ_GU ? !h_act : !out) || (bounds == nullptr && n_groups != 1) || act < 0 || act > 2)
+        return fail(TSB_ERR_ARG, "moe_prefill: arguments");
+    if ((uintptr_t) x_act % 256 || (mode == MQ_GU ? (uintptr_t) h_act % 256 : (uintptr_t) out % 16))
+        return fail(TSB_ERR_ALIGN, "moe_prefill: activation buffers 256-byte aligned, outputs 16-byte aligned");
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    MqParams pp = mq_params(L, mode, blobs, blob_stride, bounds, n_groups, n_rows);
+    pp.err = di->err;
+    pp.dbg = dbg;
     pp.act = act;
     pp.limit = limit;
-    return pf_launch(PF_GU, L->gu_type, pp, cs(stream));
+    const MmqView xa = mmq_view(x_act, n_rows, pp.K);
+    if (mode == MQ_GU) {
+        const MmqView ha = mmq_view(h_act, n_rows, pp.N);
+        pp.hc = ha.codes;
+        pp.hd = ha.d;
+        pp.hs = ha.s;
+        pp.ldh = ha.ldS;
+        return mq_launch<MQ_GU>(L->gu_type, pp, xa, s, di);
+    }
+    pp.D = out;
+    return mq_launch<MQ_DOWN>(L->d_type, pp, xa, s, di);
+}
+
+extern "C" {
+
+int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
+                       int n_groups, int n_rows, const void* x_act, void* h_act, int act, float limit, void* stream) {
+    return mq_run(L, MQ_GU, blobs, blob_stride, bounds, n_groups, n_rows, x_act, h_act, nullptr, act, limit, nullptr,
+                  cs(stream));
 }
 
 int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
-                         int n_groups, int n_rows, const void* h_q8_1, float* out, void* stream) {
-    int rc = pf_check(L, blobs, blob_stride, n_groups, n_rows, PF_DOWN);
-    if (rc != TSB_OK) return rc;
-    if (n_rows == 0) return TSB_OK;
-    if (!h_q8_1 || !out || (bounds == nullptr && n_groups != 1)) return fail(TSB_ERR_ARG, "moe_prefill_down: arguments");
-    if ((uintptr_t) h_q8_1 % 4 || (uintptr_t) out % 16) return fail(TSB_ERR_ALIGN, "moe_prefill_down: alignment");
-    PfParams pp{};
-    pp.bounds = bounds;
-    pp.n_groups = n_groups;
-    pp.n_rows = n_rows;
-    pp.blobs = (const uint8_t*) blobs;
-    pp.blob_stride = blob_stride;
-    pp.w_off = L->down_off;
-    pp.w_row = (uint32_t) L->d_row;
-    pp.K = (int) L->n_ff;
-    pp.N = (int) L->n_embd;
-    pp.X = (const BlockQ8_1*) h_q8_1;
-    pp.D = out;
-    return pf_launch(PF_DOWN, L->d_type, pp, cs(stream));
+                         int n_groups, int n_rows, const void* h_act, float* out, void* stream) {
+    return mq_run(L, MQ_DOWN, blobs, blob_stride, bounds, n_groups, n_rows, h_act, nullptr, out, ACT_SWIGLU, INFINITY,
+                  nullptr, cs(stream));
 }
 
+int tsb_debug_mmq_block_sums(const tsb_expert_layout* L, int mode, const void* blob, int n_rows, const void* x_act,
+                             void* h_act, float* out, int32_t* sums, void* stream) {
+    if (!sums || (mode != MQ_GU && mode != MQ_DOWN)) return fail(TSB_ERR_ARG, "debug_mmq_block_sums: arguments");
+    return mq_run(L, mode, blob, L ? L->bytes : 0, nullptr, 1, n_rows, x_act, h_act, out, ACT_SWIGLU, INFINITY, sums,
+                  cs(stream));
+}
+
+}  // extern "C"
+
+extern "C" {
 // ------------------------------------------------------------------------------------ no-allocation grouped experts
 // tsb_native_expert_grouped with its scratch (the entries' hidden vectors, fp32 [cap_entries][n_ff]) in a fixed
 // device array of this library instead of a caller buffer.  The array is zero when the module loads and needs no

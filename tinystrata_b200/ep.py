@@ -101,7 +101,8 @@ def gpu_expert_fn(L, blobs, blob_stride: int, act: int, limit: float = float("in
         R, K = rids.shape
         bounds, row_ent, row_tok, rinv = T.moe_dispatch(rids, n_local, stream=stream)
         n = int(bounds[-1].item())
-        h = T.moe_prefill_gu(L, blobs, blob_stride, bounds, n_local, n, rows, row_tok, act, limit, stream=stream)
+        xa = T.mmq_from_q8_1(rows, int(L.n_embd), row_src=row_tok, n_rows=n, stream=stream)
+        h = T.moe_prefill_gu(L, blobs, blob_stride, bounds, n_local, n, xa, act, limit, stream=stream)
         parts = T.moe_prefill_down(L, blobs, blob_stride, bounds, n_local, n, h, stream=stream)
         valid = rinv.view(R, K) >= 0
         idx = torch.where(valid, rinv.view(R, K), torch.zeros_like(rinv.view(R, K))).long()

@@ -112,7 +112,7 @@ class PrefillLayer:
 
     def __init__(self, cfg: dict, blobs, router, sh_blob=None, max_tokens: int = 8192, escale=None, bias=None):
         import torch
-        from . import (Q8_1_BYTES, native_expert_layout)
+        from . import MmqAct, native_expert_layout
         self.cfg = cfg
         self.H, self.F, self.E, self.K = cfg["n_embd"], cfg["n_ff"], cfg["n_expert"], cfg["n_used"]
         self.blobs, self.router, self.sh_blob = blobs, router.contiguous(), sh_blob
@@ -121,19 +121,21 @@ class PrefillLayer:
         self.escale, self.bias = escale, bias
         dev = blobs.device
         T, K, H = max_tokens, self.K, self.H
+        self.max_tokens = T
         self.logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
-        self.xq = torch.empty((T, H // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
-        self.hq = torch.empty((T * K, self.F // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
+        self.xa = MmqAct(T * K, H, dev)            # the routed rows in expert order (tensor-core layout)
+        self.ha = MmqAct(T * K, self.F, dev)       # their hidden vectors
         self.parts = torch.empty((T * K, H), dtype=torch.float32, device=dev)
         self.Ls = None
         if sh_blob is not None and cfg.get("sh_n_ff"):
             self.Ls = native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, cfg["sh_n_ff"])
-            self.sh_hq = torch.empty((T, cfg["sh_n_ff"] // 32 * Q8_1_BYTES), dtype=torch.uint8, device=dev)
+            self.xs = MmqAct(T, H, dev)
+            self.hs = MmqAct(T, cfg["sh_n_ff"], dev)
             self.shared = torch.empty((T, H), dtype=torch.float32, device=dev)
 
     def forward(self, x, h, stream=None):
         """x += MoE(h) for T = x.shape[0] tokens (h fp32 [T, H], the layer's normed input)."""
-        from . import (moe_combine, moe_dispatch, moe_prefill_down, moe_prefill_gu, quantize_q8_1_rows, route_rows,
+        from . import (MmqAct, mmq_quantize, moe_combine, moe_dispatch, moe_prefill_down, moe_prefill_gu, route_rows,
                        router_logits_f32)
         cfg = self.cfg
         T = x.shape[0]
@@ -143,17 +145,23 @@ class PrefillLayer:
             ids, w = route_rows(logits, K, 0, cfg.get("in_scale", 1.0), None, self.escale, True, 0.0, stream=stream)
         else:
             ids, w = route_rows(logits, K, 1, 1.0, self.bias, None, True, cfg.get("w_scale", 0.0), stream=stream)
-        xq = quantize_q8_1_rows(h, self.xq[:T], stream=stream)
         bounds, row_ent, row_tok, rinv = moe_dispatch(ids, E, stream=stream)
         n = T * K
-        hq = moe_prefill_gu(self.L, self.blobs, self.stride, bounds, E, n, xq, row_tok, cfg["act"],
-                            cfg.get("limit", float("inf")), h=self.hq[:n], stream=stream)
-        parts = moe_prefill_down(self.L, self.blobs, self.stride, bounds, E, n, hq, out=self.parts[:n], stream=stream)
+        xa = self.xa if T == self.max_tokens else MmqAct(n, self.H, x.device, buf=self.xa._store)
+        ha = self.ha if T == self.max_tokens else MmqAct(n, self.F, x.device, buf=self.ha._store)
+        mmq_quantize(h, row_src=row_tok, n_rows=n, out=xa, stream=stream)
+        moe_prefill_gu(self.L, self.blobs, self.stride, bounds, E, n, xa, cfg["act"], cfg.get("limit", float("inf")),
+                       h=ha, stream=stream)
+        parts = moe_prefill_down(self.L, self.blobs, self.stride, bounds, E, n, ha, out=self.parts[:n], stream=stream)
         shared = None
         if self.Ls is not None:
-            sh = moe_prefill_gu(self.Ls, self.sh_blob, 0, None, 1, T, xq, None, cfg.get("sh_act", cfg["act"]),
-                                cfg.get("limit", float("inf")), h=self.sh_hq[:T], stream=stream)
-            shared = moe_prefill_down(self.Ls, self.sh_blob, 0, None, 1, T, sh, out=self.shared[:T], stream=stream)
+            FS = self.cfg["sh_n_ff"]
+            xs = self.xs if T == self.max_tokens else MmqAct(T, self.H, x.device, buf=self.xs._store)
+            hs = self.hs if T == self.max_tokens else MmqAct(T, FS, x.device, buf=self.hs._store)
+            mmq_quantize(h, n_rows=T, out=xs, stream=stream)
+            moe_prefill_gu(self.Ls, self.sh_blob, 0, None, 1, T, xs, cfg.get("sh_act", cfg["act"]),
+                           cfg.get("limit", float("inf")), h=hs, stream=stream)
+            shared = moe_prefill_down(self.Ls, self.sh_blob, 0, None, 1, T, hs, out=self.shared[:T], stream=stream)
         moe_combine(x, parts, w, K, shared=shared, prow=rinv, stream=stream)
-        self.ids, self.w, self.rinv = ids, w, rinv
+        self.ids, self.w, self.rinv, self.bounds = ids, w, rinv, bounds
         return x
