@@ -14,8 +14,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsb_moe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 SOURCES = ["tsb_moe.cu", "tsb_decode.cu"]
-HEADERS = ["tsb_device.cuh", "tsb_formats.cuh", "tsb_kernels.cuh", "tsb_decode.cuh", "tsb_prefill.cuh", "tsb_prefill_k.cuh", "codebooks.inc",
-           "../../include/tsb_moe.h"]
+# every header of the sources: a change to any of them rebuilds both objects
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cuh", ".inc"))) + ["../../include/tsb_moe.h"]
 FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",
          "--expt-relaxed-constexpr"]
 

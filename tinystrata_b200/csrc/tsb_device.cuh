@@ -205,6 +205,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// The same with test_wait polls (never suspended): for a wait on the critical path whose phase usually completes within
+// a few hundred cycles, where try_wait's suspension can oversleep the completion.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, unsigned* err, unsigned site) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer(), lim = wait_limit_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 1023u) == 0 && globaltimer() - t0 > lim) {
+            report_error(err, site);
+            return false;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------------------------- tables
 // The IQ3_XXS grid and the sign masks of a 7-bit sign index, lane-banked in 64 KB of shared memory so that 32 lanes
 // reading 32 different entries never share a bank:

@@ -764,30 +764,50 @@ __global__ void __launch_bounds__(kMqThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ activations
-// fp32 rows -> the mmq layout: row r of the output is source row src[r] (null: r) of x (row stride ld_x floats), one
-// warp per 32-value block (the reference's q8_1 quantiser: amax / 127 with the fast-math division, roundf, clamp),
-// codes [rows][K], d [rows][ldS] (the fp16-rounded scale), s [rows][ldS] = d * sum of the codes.
+// fp32 rows -> the mmq layout: row r of the output is source row src[r] (null: r) of x (row stride ld_x floats); one
+// CTA per output row, eight lanes per 32-value block with four values each (16-byte loads, 4-byte code stores).  The
+// reference's q8_1 quantiser (iq_kernels.cu:1469-1480): d = amax / 127 with the fast-math division, codes roundf(x / d)
+// clamped to +-127 -- the same codes and fp16 scale whatever the lane layout; codes [rows][K], d [rows][ldS] (the
+// fp16-rounded scale), s [rows][ldS] = d * sum of the codes.
 __global__ void __launch_bounds__(256) k_mmq_quantize(const float* __restrict__ x, long long ld_x,
                                                       const int32_t* __restrict__ src, int n_rows, int K,
                                                       int8_t* __restrict__ codes, float* __restrict__ ds,
                                                       float* __restrict__ ss, int ldS) {
-    const int nb = K / 32;
-    const long long wid = (long long) blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (wid >= (long long) n_rows * nb) return;
-    const int lane = threadIdx.x & 31;
-    const int r = (int) (wid / nb), b = (int) (wid % nb);
+    const int r = blockIdx.x;
     const int sr = src ? __ldg(src + r) : r;
-    const float v = __ldg(x + (size_t) sr * ld_x + 32 * b + lane);
-    float d, sum;
-    const int8_t qv = q8_1_warp(v, d, sum);
-    codes[(size_t) r * K + 32 * b + lane] = qv;
-    int cs = qv;
+    const float4* xr = (const float4*) (x + (size_t) sr * ld_x);
+    uint32_t* cr = (uint32_t*) (codes + (size_t) r * K);
+    const int lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i - lane < K / 4; i += blockDim.x) {   // whole warps: 8 blocks of 32 values a pass
+        const bool in = i < K / 4;
+        const float4 v = in ? __ldg(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
-    if (lane == 0) {
-        const float dh = __half2float(__float2half(q8_finite(d)));
-        ds[(size_t) r * ldS + b] = dh;
-        ss[(size_t) r * ldS + b] = dh * (float) cs;
+        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = q8_finite(fdiv_fm(amax, 127.0f));
+        const float xs[4] = {v.x, v.y, v.z, v.w};
+        uint32_t word = 0;
+        int cs = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int c = 0;
+            if (amax != 0.0f) {
+                const float rq = roundf(fdiv_fm(xs[j], d));
+                c = (int) (rq > 127.0f ? 127.0f : rq < -127.0f ? -127.0f : rq);
+            }
+            cs += c;
+            word |= (uint32_t) (uint8_t) (int8_t) c << (8 * j);
+        }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) cs += __shfl_xor_sync(0xffffffffu, cs, o);
+        if (in) {
+            cr[i] = word;
+            if ((lane & 7) == 0) {
+                const float dh = __half2float(__float2half(d));
+                ds[(size_t) r * ldS + (i >> 3)] = dh;
+                ss[(size_t) r * ldS + (i >> 3)] = dh * (float) cs;
+            }
+        }
     }
 }
 // q8_1 blocks -> the mmq layout (the same codes and scales), row r from source row src[r] (null: r).

@@ -382,6 +382,41 @@ __global__ void __launch_bounds__(1024) k_combine(float* __restrict__ x, const f
     }
 }
 
+// The combine without the norm epilogue (the prompt path): the same per-value expressions in the same order as
+// k_combine, four values a thread (16-byte loads and stores), 256 threads a token row.
+__global__ void __launch_bounds__(256) k_combine_v4(float* __restrict__ x, const float* __restrict__ parts,
+                                                    const int32_t* __restrict__ prow, const float* __restrict__ wts,
+                                                    int K, const float* __restrict__ shared,
+                                                    const float* __restrict__ sgate, int sg_stride, int n) {
+    __shared__ const float4* pk[32];
+    __shared__ float ws[32];
+    const int t = blockIdx.x;
+    if ((int) threadIdx.x < K) {
+        pk[threadIdx.x] = (const float4*) (parts + (size_t) (prow ? __ldg(prow + t * K + threadIdx.x)
+                                                                   : t * K + threadIdx.x) * n);
+        ws[threadIdx.x] = __ldg(wts + (size_t) t * K + threadIdx.x);
+    }
+    __syncthreads();
+    const float gs = sgate ? frcp_fm(1.0f + fexp_fm(-sgate[(size_t) t * sg_stride])) : 1.0f;
+    float4* xr = (float4*) (x + (size_t) t * n);
+    const float4* sr = shared ? (const float4*) (shared + (size_t) t * n) : nullptr;
+    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
+        float4 p = __ldcs(pk[0] + i);
+        float4 acc = make_float4(ws[0] * p.x, ws[0] * p.y, ws[0] * p.z, ws[0] * p.w);
+        for (int k = 1; k < K; ++k) {
+            p = __ldcs(pk[k] + i);
+            acc = make_float4(fmaf(ws[k], p.x, acc.x), fmaf(ws[k], p.y, acc.y), fmaf(ws[k], p.z, acc.z),
+                              fmaf(ws[k], p.w, acc.w));
+        }
+        if (sr) {
+            const float4 v = __ldcs(sr + i);
+            acc = make_float4(acc.x + gs * v.x, acc.y + gs * v.y, acc.z + gs * v.z, acc.w + gs * v.w);
+        }
+        const float4 xv = xr[i];
+        xr[i] = make_float4(xv.x + acc.x, xv.y + acc.y, xv.z + acc.z, xv.w + acc.w);
+    }
+}
+
 // h = x * rsqrt(mean(x^2) + eps) * wn and hq = q8_1(h), one CTA of 1024 per row: the combine's epilogue alone (the
 // reference's k_add_rms_q without the add, q36_kernels.cuh:222-250).
 __global__ void __launch_bounds__(1024) k_rms_q8_1(const float* __restrict__ x, const float* __restrict__ wn,
@@ -796,6 +831,11 @@ int tsb_moe_combine(float* x, const float* parts, const int32_t* prow, const flo
     if (n_tok <= 0) return TSB_OK;
     if (!x || !parts || !wts || K < 1 || K > 32 || n % 32 != 0 || n <= 0)
         return fail(TSB_ERR_ARG, "moe_combine: arguments");
+    if (!wn && !h && !hq && n % 4 == 0 && (uintptr_t) x % 16 == 0 && (uintptr_t) parts % 16 == 0 &&
+        (!shared || (uintptr_t) shared % 16 == 0)) {   // no norm epilogue: the vectorised combine
+        k_combine_v4<<<n_tok, 256, 0, cs(stream)>>>(x, parts, prow, wts, K, shared, sgate, sg_stride, n);
+        return cuda_status("moe_combine");
+    }
     const size_t sh = sizeof(float) * ((size_t) n + 256);
     if (sh > 200 * 1024) return fail(TSB_ERR_UNSUPPORTED, "moe_combine: n %d too large", n);
     if (sh > 48 * 1024 &&
@@ -930,10 +970,9 @@ int tsb_mmq_quantize(const float* x, int64_t ld_x, const int32_t* row_src, int n
     if (n_rows == 0) return TSB_OK;
     if (!x || !act || n_rows < 0 || K <= 0 || K % 32 || ld_x < K) return fail(TSB_ERR_ARG, "mmq_quantize: arguments");
     if ((uintptr_t) act % 256) return fail(TSB_ERR_ALIGN, "mmq_quantize: the activation buffer must be 256-byte aligned");
+    if ((uintptr_t) x % 16 || ld_x % 4) return fail(TSB_ERR_ALIGN, "mmq_quantize: 16-byte aligned rows");
     const MmqView v = mmq_view(act, n_rows, K);
-    const long long warps = (long long) n_rows * (K / 32);
-    k_mmq_quantize<<<(unsigned) ((warps + 7) / 8), 256, 0, cs(stream)>>>(x, ld_x, row_src, n_rows, K, v.codes, v.d, v.s,
-                                                                          v.ldS);
+    k_mmq_quantize<<<(unsigned) n_rows, 256, 0, cs(stream)>>>(x, ld_x, row_src, n_rows, K, v.codes, v.d, v.s, v.ldS);
     return cuda_status("mmq_quantize");
 }
 

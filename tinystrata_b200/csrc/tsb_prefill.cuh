@@ -553,37 +553,43 @@ __global__ void __launch_bounds__(1024) k_dispatch_count(const int32_t* __restri
     }
 }
 // One CTA per expert: its entries in entry order (a stable sort by expert) -> rows bounds[e]...; row_ent[row] = entry,
-// row_tok[row] = entry / K, rinv[entry] = row.
+// row_tok[row] = entry / K, rinv[entry] = row.  Each of the 32 warps owns a contiguous segment of the entries and scans
+// it twice with coalesced loads: once to count the expert's entries (ballots), then, after an exclusive scan of the 32
+// warp counts, to write them in order (a lane's rank is the popcount of the lanes below it in its ballot).
 __global__ void __launch_bounds__(1024) k_dispatch_scatter(const int32_t* __restrict__ ids, int n_ent, int K,
                                                            const int32_t* __restrict__ bounds,
                                                            int32_t* __restrict__ row_ent, int32_t* __restrict__ row_tok,
                                                            int32_t* __restrict__ rinv) {
-    __shared__ int32_t wsum[32];
-    __shared__ int32_t base_s;
+    __shared__ int32_t wbase[33];
     const int e = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) base_s = bounds[e];
+    const int seg = (n_ent + 32 * 32 - 1) / (32 * 32) * 32;   // entries a warp owns (a multiple of 32)
+    const int lo = warp * seg, hi = min(lo + seg, n_ent);
+    int cnt = 0;
+    for (int i0 = lo; i0 < hi; i0 += 32) {
+        const int i = i0 + lane;
+        cnt += __popc(__ballot_sync(0xffffffffu, i < hi && __ldg(ids + i) == e));
+    }
+    if (lane == 0) wbase[warp + 1] = cnt;
     __syncthreads();
-    for (int i0 = 0; i0 < n_ent; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const bool f = i < n_ent && ids[i] == e;
+    if (threadIdx.x == 0) {
+        wbase[0] = bounds[e];
+        for (int w = 0; w < 32; ++w) wbase[w + 1] += wbase[w];
+    }
+    __syncthreads();
+    int base = wbase[warp];
+    const unsigned below = (1u << lane) - 1u;
+    for (int i0 = lo; i0 < hi && base < wbase[warp + 1]; i0 += 32) {
+        const int i = i0 + lane;
+        const bool f = i < hi && __ldg(ids + i) == e;
         const unsigned m = __ballot_sync(0xffffffffu, f);
-        if (lane == 0) wsum[warp] = __popc(m);
-        __syncthreads();
-        int before = 0, total = 0;
-        for (int w = 0; w < (int) (blockDim.x >> 5); ++w) {
-            before += w < warp ? wsum[w] : 0;
-            total += wsum[w];
-        }
         if (f) {
-            const int row = base_s + before + __popc(m & ((1u << lane) - 1u));
+            const int row = base + __popc(m & below);
             row_ent[row] = i;
             row_tok[row] = i / K;
             rinv[i] = row;
         }
-        __syncthreads();
-        if (threadIdx.x == 0) base_s += total;
-        __syncthreads();
+        base += __popc(m);
     }
 }
 
