@@ -180,6 +180,21 @@ int tsb_rms_norm_q8_1(const float* x, const float* wn, float* h, void* hq, int n
 /* acc[t] += sum_k w[t,k] x[t*K+k], n values per row.  Replaces moe_sum (src/gemma4/kernels.cu:358-366). */
 int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, int rows, void* stream);
 
+/* Up to 32 scaled vectors added into sums: acc[k][i] += x[k][i] * w[k] for k in order (the sums may be one and the same
+ * vector).  Replaces add_scaled and its ScaledRows (include/strata/gemma4/kernels.hpp:51-56, src/gemma4/kernels.cu:
+ * 245-249, 1444-1447): the host structure holds device pointers and the weights. */
+typedef struct tsb_scaled_rows {
+    const float* x[32];
+    float* acc[32];
+    float w[32];
+} tsb_scaled_rows;
+int tsb_add_scaled(const tsb_scaled_rows* rows, int count, int n, void* stream);
+/* The Gemma 4 layer tail after the routed experts, per row of n values: cur = rms(moe) * post_moe + mlp (mlp may be
+ * null), out = rms(cur) * post_ffn, r = (r + out) * out_scale (norm weights may be null: 1).  Replaces the
+ * rms_norm / axpy / rms_norm / axpy / scale sequence of Gemma4::layer_tail (src/gemma4/gemma4.cpp:560-568). */
+int tsb_moe_layer_tail(const float* moe, const float* post_moe, const float* mlp, const float* post_ffn, float* r,
+                       float out_scale, int n, int rows, float eps, void* stream);
+
 /* --------------------------------------------------------------------------------------------- fused decode */
 /* One layer of the fused decode path: device pointers to its expert blobs ([n_expert][blob bytes], the
  * NativeExpertLayout of each), its fp32 router ([n_expert + 1][n_embd]: the expert rows, then the shared-expert gate

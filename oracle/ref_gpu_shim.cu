@@ -9,6 +9,8 @@
 //   native_expert_layout ...... include/strata/kernels/iq_kernels.hpp:53
 //   native_expert_grouped ..... include/strata/kernels/iq_kernels.hpp:75-78
 //   k_moe_out_small ........... src/qwen35/q36_kernels.cuh:252-290 (header-only kernel, instantiated here)
+//   route_rows, moe_sum, add_scaled ... include/strata/gemma4/kernels.hpp:43-56 (src/gemma4/kernels.cu)
+#include "strata/gemma4/kernels.hpp"
 #include "strata/kernels/iq_kernels.hpp"
 #include "strata/kernels/native_router.hpp"
 #include "q36_kernels.cuh"
@@ -19,6 +21,36 @@
 namespace sk = strata::kernels;
 
 extern "C" {
+
+int ref_route_rows(const float* logits, int n_expert, int n_used, int rows, int gate, float in_scale, const float* bias,
+                   const float* escale, int norm, float w_scale, int32_t* ids, float* w, void* stream) {
+    try {
+        strata::gemma4::route_rows(logits, n_expert, n_used, rows, gate, in_scale, bias, escale, norm != 0, w_scale,
+                                   ids, w, stream);
+    } catch (const std::exception&) {
+        return -1;
+    }
+    return 0;
+}
+
+void ref_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, int rows, void* stream) {
+    strata::gemma4::moe_sum(x, w, acc, n, n_used, rows, stream);
+}
+
+int ref_add_scaled(const float* const* x, float* const* acc, const float* w, int count, int n, void* stream) {
+    strata::gemma4::ScaledRows r{};
+    for (int k = 0; k < count && k < 32; ++k) {
+        r.x[k] = x[k];
+        r.acc[k] = acc[k];
+        r.w[k] = w[k];
+    }
+    try {
+        strata::gemma4::add_scaled(r, count, n, stream);
+    } catch (const std::exception&) {
+        return -1;
+    }
+    return 0;
+}
 
 int ref_native_router_topk(const float* logits, int32_t* ids, float* w, int n_expert, int k, int n_tok, void* stream) {
     try {

@@ -29,6 +29,12 @@ def lib():
         L.ref_moe_out_small.argtypes = [_p, _p, _p, _p, C.c_int, _p, _p, C.c_int, _p, _p, C.c_int, C.c_float, _p,
                                         C.c_int, _p]
         L.ref_last_cuda_error.restype = C.c_int
+        L.ref_route_rows.restype = C.c_int
+        L.ref_route_rows.argtypes = [_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _p, _p, C.c_int, C.c_float, _p,
+                                     _p, _p]
+        L.ref_moe_sum.argtypes = [_p, _p, _p, C.c_int, C.c_int, C.c_int, _p]
+        L.ref_add_scaled.restype = C.c_int
+        L.ref_add_scaled.argtypes = [_p, _p, _p, C.c_int, C.c_int, _p]
         _lib = L
     return _lib
 

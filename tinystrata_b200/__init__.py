@@ -86,6 +86,8 @@ SIGNATURES = {
     "tsb_decode_last_error": (C.c_char_p, []),
     "tsb_moe_decode_set_trace": (C.c_int, [_p]),
     "tsb_moe_decode_set_debug": (C.c_int, [C.c_int]),
+    "tsb_add_scaled": (C.c_int, [_p, C.c_int, C.c_int, _p]),
+    "tsb_moe_layer_tail": (C.c_int, [_p, _p, _p, _p, _p, _f, C.c_int, C.c_int, _f, _p]),
     "tsb_set_wait_limit_ns": (C.c_int, [_u64]),
 }
 
@@ -379,6 +381,27 @@ def moe_sum(x, w, acc, n_used, stream=None):
     rows, n = acc.shape
     _check(lib().tsb_moe_sum(_ptr(x), _ptr(w), _ptr(acc), n, n_used, rows, _stream(stream)), "moe_sum")
     return acc
+
+
+class ScaledRows(C.Structure):
+    """tsb_scaled_rows (the reference's ScaledRows, include/strata/gemma4/kernels.hpp:51-56)."""
+    _fields_ = [("x", C.c_void_p * 32), ("acc", C.c_void_p * 32), ("w", C.c_float * 32)]
+
+
+def add_scaled(xs, accs, ws, stream=None):
+    """accs[k] += xs[k] * ws[k] for k in order (add_scaled, src/gemma4/kernels.cu:245-249)."""
+    R = ScaledRows()
+    for k, (x, a, w) in enumerate(zip(xs, accs, ws)):
+        R.x[k], R.acc[k], R.w[k] = x.data_ptr(), a.data_ptr(), float(w)
+    _check(lib().tsb_add_scaled(C.byref(R), len(xs), xs[0].numel(), _stream(stream)), "add_scaled")
+
+
+def moe_layer_tail(moe, r, post_moe=None, mlp=None, post_ffn=None, out_scale=1.0, eps=1e-6, stream=None):
+    """The Gemma 4 layer tail (gemma4.cpp:560-568): r = (r + rms(rms(moe) post_moe + mlp) post_ffn) out_scale."""
+    rows, n = moe.shape
+    _check(lib().tsb_moe_layer_tail(_ptr(moe), _ptr(post_moe), _ptr(mlp), _ptr(post_ffn), _ptr(r), out_scale, n, rows,
+                                    eps, _stream(stream)), "moe_layer_tail")
+    return r
 
 
 def debug_row_calls(ggml_type: int, row, x_q8_1, n: int, stream=None):

@@ -458,6 +458,50 @@ __global__ void k_moe_sum(const float* __restrict__ x, const float* __restrict__
     acc[(size_t) blockIdx.y * n + i] += s;
 }
 
+// acc[k][i] += x[k][i] * w[k] for k in order (the sums may alias: a thread adds its value of each vector in turn), the
+// reference's add_scaled (src/gemma4/kernels.cu:245-249).
+__global__ void k_add_scaled(tsb_scaled_rows rows, int count, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    for (int k = 0; k < count; ++k) rows.acc[k][i] = fmaf(rows.x[k][i], rows.w[k], rows.acc[k][i]);
+}
+
+// Sum of squares of one row, 256 threads: thread t adds values t, t + 256, ... in order, then a halving tree.
+__device__ __forceinline__ float row_sumsq(const float* __restrict__ x, int n, float* red) {
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) s = fmaf(x[i], x[i], s);
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+        if ((int) threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+        __syncthreads();
+    }
+    const float v = red[0];
+    __syncthreads();
+    return v;
+}
+// The Gemma 4 layer tail after the routed experts (src/gemma4/gemma4.cpp:560-568), one row per CTA:
+// cur = rms(moe) * post_moe (+ mlp); out = rms(cur) * post_ffn; r += out; r *= out_scale.  `cur` lives in shared memory.
+__global__ void __launch_bounds__(256) k_layer_tail(const float* __restrict__ moe, const float* __restrict__ post_moe,
+                                                    const float* __restrict__ mlp, const float* __restrict__ post_ffn,
+                                                    float* __restrict__ r, float out_scale, int n, float eps) {
+    extern __shared__ float cur[];   // n values, then 256 partial sums
+    float* red = cur + n;
+    const size_t off = (size_t) blockIdx.x * n;
+    const float r1 = rsqrtf(row_sumsq(moe + off, n, red) / (float) n + eps);
+    for (int i = threadIdx.x; i < n; i += 256) {
+        float v = moe[off + i] * r1 * (post_moe ? post_moe[i] : 1.0f);
+        if (mlp) v += mlp[off + i];
+        cur[i] = v;
+    }
+    __syncthreads();
+    const float r2 = rsqrtf(row_sumsq(cur, n, red) / (float) n + eps);
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float o = cur[i] * r2 * (post_ffn ? post_ffn[i] : 1.0f);
+        r[off + i] = (r[off + i] + o) * out_scale;
+    }
+}
+
 // Test hook: the per-call integer sums and float values of one row against one q8_1 activation.
 template <int TY>
 __global__ void k_row_calls(const uint8_t* __restrict__ row, const BlockQ8_1* __restrict__ x, int n_calls,
@@ -858,6 +902,28 @@ int tsb_moe_sum(const float* x, const float* w, float* acc, int n, int n_used, i
     if (!x || !w || !acc || n <= 0 || n_used < 1) return fail(TSB_ERR_ARG, "moe_sum: arguments");
     k_moe_sum<<<dim3((unsigned) ((n + 255) / 256), (unsigned) rows), 256, 0, cs(stream)>>>(x, w, acc, n, n_used);
     return cuda_status("moe_sum");
+}
+
+int tsb_add_scaled(const tsb_scaled_rows* rows, int count, int n, void* stream) {
+    if (n <= 0) return TSB_OK;
+    if (!rows || count < 1 || count > 32) return fail(TSB_ERR_ARG, "add_scaled: 1 to 32 vectors");
+    for (int k = 0; k < count; ++k)
+        if (!rows->x[k] || !rows->acc[k]) return fail(TSB_ERR_ARG, "add_scaled: null vector %d", k);
+    k_add_scaled<<<(unsigned) ((n + 255) / 256), 256, 0, cs(stream)>>>(*rows, count, n);
+    return cuda_status("add_scaled");
+}
+
+int tsb_moe_layer_tail(const float* moe, const float* post_moe, const float* mlp, const float* post_ffn, float* r,
+                       float out_scale, int n, int rows, float eps, void* stream) {
+    if (rows <= 0) return TSB_OK;
+    if (!moe || !r || n <= 0) return fail(TSB_ERR_ARG, "moe_layer_tail: arguments");
+    const size_t sh = sizeof(float) * ((size_t) n + 256);
+    if (sh > 200 * 1024) return fail(TSB_ERR_UNSUPPORTED, "moe_layer_tail: n %d too large", n);
+    if (sh > 48 * 1024 &&
+        cudaFuncSetAttribute(k_layer_tail, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) sh) != cudaSuccess)
+        return cuda_status("moe_layer_tail: shared memory");
+    k_layer_tail<<<(unsigned) rows, 256, sh, cs(stream)>>>(moe, post_moe, mlp, post_ffn, r, out_scale, n, eps);
+    return cuda_status("moe_layer_tail");
 }
 
 // ------------------------------------------------------------------------------------------------ prefill
