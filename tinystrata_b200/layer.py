@@ -122,7 +122,10 @@ class PrefillLayer:
         dev = blobs.device
         T, K, H = max_tokens, self.K, self.H
         self.max_tokens = T
-        self.logits = torch.empty((T, self.E), dtype=torch.float32, device=dev)
+        self.rows = self.router.shape[0]         # E, or E + 1 with Qwen's shared-expert gate row
+        self.logits = torch.empty((T, self.rows), dtype=torch.float32, device=dev)
+        self._ids = torch.empty((T, self.K), dtype=torch.int32, device=dev)
+        self._w = torch.empty((T, self.K), dtype=torch.float32, device=dev)
         self.xa = MmqAct(T * K, H, dev)            # the routed rows in expert order (tensor-core layout)
         self.ha = MmqAct(T * K, self.F, dev)       # their hidden vectors
         self.parts = torch.empty((T * K, H), dtype=torch.float32, device=dev)
@@ -133,18 +136,30 @@ class PrefillLayer:
             self.hs = MmqAct(T, cfg["sh_n_ff"], dev)
             self.shared = torch.empty((T, H), dtype=torch.float32, device=dev)
 
-    def forward(self, x, h, stream=None):
-        """x += MoE(h) for T = x.shape[0] tokens (h fp32 [T, H], the layer's normed input)."""
-        from . import (MmqAct, mmq_quantize, moe_combine, moe_dispatch, moe_prefill_down, moe_prefill_gu, route_rows,
-                       router_logits_f32)
+    def forward(self, x, h, stream=None, h_next=None, hq_next=None, eps: float = 1e-6, prior=None):
+        """x += MoE(h) for T = x.shape[0] tokens (h fp32 [T, H], the layer's normed input).  Qwen's routing
+        (router_mode "softmax": softmax top-k, q36_engine.cu:2821-2840) gates the shared expert by the sigmoid of the
+        router's extra row, and with h_next / hq_next also writes the next layer's normed input and its q8_1 image
+        (k_moe_out, q36_engine.cu:307-332); Gemma / LFM2 route by route_rows.  prior (optional, [T, E]) is added to
+        the router logits before routing, as MoELayer's."""
+        from . import (MmqAct, mmq_quantize, moe_combine, moe_dispatch, moe_prefill_down, moe_prefill_gu,
+                       native_router_topk, route_rows, router_logits_f32)
         cfg = self.cfg
         T = x.shape[0]
         K, E = self.K, self.E
-        logits = router_logits_f32(self.router[:E], h, self.logits[:T], stream=stream)
-        if cfg["router_mode"] == "softmax_scaled":
-            ids, w = route_rows(logits, K, 0, cfg.get("in_scale", 1.0), None, self.escale, True, 0.0, stream=stream)
+        mode = cfg["router_mode"]
+        logits = router_logits_f32(self.router, h, self.logits[:T], ld=self.rows, stream=stream)
+        if prior is not None:
+            with torch.cuda.stream(stream) if stream is not None else torch.cuda.stream(torch.cuda.current_stream()):
+                logits[:, :E].add_(prior)
+        if mode == "softmax":
+            ids, w = native_router_topk(logits, K, E, self._ids[:T], self._w[:T], stream=stream)
+        elif mode == "softmax_scaled":
+            ids, w = route_rows(logits[:, :E].contiguous(), K, 0, cfg.get("in_scale", 1.0), None, self.escale, True,
+                                0.0, stream=stream)
         else:
-            ids, w = route_rows(logits, K, 1, 1.0, self.bias, None, True, cfg.get("w_scale", 0.0), stream=stream)
+            ids, w = route_rows(logits[:, :E].contiguous(), K, 1, 1.0, self.bias, None, True, cfg.get("w_scale", 0.0),
+                                stream=stream)
         bounds, row_ent, row_tok, rinv = moe_dispatch(ids, E, stream=stream)
         n = T * K
         xa = self.xa if T == self.max_tokens else MmqAct(n, self.H, x.device, buf=self.xa._store)
@@ -162,6 +177,8 @@ class PrefillLayer:
             moe_prefill_gu(self.Ls, self.sh_blob, 0, None, 1, T, xs, cfg.get("sh_act", cfg["act"]),
                            cfg.get("limit", float("inf")), h=hs, stream=stream)
             shared = moe_prefill_down(self.Ls, self.sh_blob, 0, None, 1, T, hs, out=self.shared[:T], stream=stream)
-        moe_combine(x, parts, w, K, shared=shared, prow=rinv, stream=stream)
+        sg = logits[:, E:] if mode == "softmax" and cfg.get("shared_gate") and shared is not None else None
+        moe_combine(x, parts, w, K, shared=shared, sgate=sg, sg_stride=self.rows, prow=rinv, h=h_next, hq=hq_next,
+                    eps=eps, stream=stream)
         self.ids, self.w, self.rinv, self.bounds = ids, w, rinv, bounds
         return x
