@@ -29,7 +29,8 @@ enum tsb_status {
     TSB_ERR_UNSUPPORTED = -2,  /* a format or shape without a kernel */
     TSB_ERR_CUDA = -3,         /* a CUDA launch or runtime error (see tsb_last_error) */
     TSB_ERR_ALIGN = -4,        /* a buffer or blob offset not aligned as the kernel needs */
-    TSB_ERR_WORKSPACE = -5     /* caller workspace smaller than the query said */
+    TSB_ERR_WORKSPACE = -5,    /* caller workspace smaller than the query said */
+    TSB_ERR_COMM = -6          /* a communicator call failed or a peer did not answer within the bound */
 };
 
 /* The layout of one expert blob: [gate rows | up rows | down rows] of raw GGUF blocks.
@@ -241,6 +242,43 @@ int tsb_moe_decode_set_trace(unsigned long long* buf);
  * router logits, so every other CTA's wait for them runs out (their site lands in the error record); 0 turns it off.
  * Process-wide.  No counterpart in the reference. */
 int tsb_moe_decode_set_debug(int withhold_cta);
+
+/* --------------------------------------------------------------------------------------------- expert parallelism */
+/* Prompt-path experts sharded over the ranks of one node (one process per GPU), dispatch and return over NCCL
+ * point-to-point exchanges on NVLink.  The reference runs one GPU per engine; the per-rank body is its prompt branch
+ * (src/gemma4/engine.cpp:2436-2457 with src/prefill/moe_mmq.cu:334-384) over the rank's experts.  Expert e lives on
+ * rank e % world as local expert e / world (cyclic) or on rank e / (n_expert / world) (block).  A token goes to a rank
+ * once, whatever number of its picks live there.  Per step one host synchronisation (the exchanged row counts); every
+ * other step of the glue (plan, pack, unpack, per-row partial sums, the ordered sum of the returns) is a kernel. */
+typedef struct tsb_ep tsb_ep;
+/* An NCCL unique id (128 bytes) for tsb_ep_create, made on one rank and handed to every rank by the caller. */
+int tsb_ep_unique_id(void* id128);
+/* Join the ranks' communicator (collective: every rank calls it with the same id) on the current device and size the
+ * buffers for max_tokens tokens per rank.  blobs: this rank's n_expert / world expert blobs (stride blob_stride) in
+ * local order.  The NCCL library the process already loaded is used (dlopen of libnccl.so.2). */
+int tsb_ep_create(const void* id128, int rank, int world, const tsb_expert_layout* L, const void* blobs,
+                  uint64_t blob_stride, int n_expert, int n_used, int cyclic, int max_tokens, int act, float limit,
+                  tsb_ep** out);
+/* Route this rank's n_tok tokens: x_q8_1 [n_tok][n_embd / 32 blocks] q8_1 rows, ids / w [n_tok][n_used] (the
+ * router's picks).  Plans and packs on `stream`, exchanges the counts (the one host synchronisation, bounded by the
+ * wait limit), and starts the dispatch exchange of every micro-batch (1..4 slices of the tokens) on the
+ * communicator's stream.  Returns once the exchanges are queued; the caller may queue more work on `stream` (the
+ * shared expert) before tsb_ep_combine. */
+int tsb_ep_dispatch(tsb_ep* ep, const void* x_q8_1, const int32_t* ids, const float* w, int n_tok, int micro_batches,
+                    void* stream);
+/* Finish the step tsb_ep_dispatch started: per micro-batch the local grouped experts on the tensor cores as its rows
+ * arrive, the weighted partial row per received token, its return exchange; then per token, on `stream`,
+ * out = (accumulate ? out : 0) + the partials of the ranks it went to in rank order (+ sigmoid(sgate[t * sg_stride])
+ * shared[t] when shared is given).  return_bf16: partial rows travel as bf16 instead of fp32. */
+int tsb_ep_combine(tsb_ep* ep, float* out, int accumulate, const float* shared, const float* sgate, int sg_stride,
+                   int return_bf16, void* stream);
+/* The bound of the host's waits on the exchanges (default 120 s): past it the communicator is aborted and the call
+ * returns TSB_ERR_COMM (the handle is then only good for tsb_ep_destroy). */
+int tsb_ep_set_timeout_ns(tsb_ep* ep, uint64_t ns);
+/* The last step's rows: rows sent to other ranks and to this one, rows received, picks computed here. */
+int tsb_ep_stats(const tsb_ep* ep, int64_t* sent, int64_t* received, int64_t* picks);
+/* Free the buffers and the communicator (collective). */
+int tsb_ep_destroy(tsb_ep* ep);
 
 /* --------------------------------------------------------------------------------------------- test hook */
 /* The per-call integer sums and float values of one weight row (n values) against one q8_1 activation, as the

@@ -87,6 +87,14 @@ SIGNATURES = {
     "tsb_moe_decode_set_trace": (C.c_int, [_p]),
     "tsb_moe_decode_set_debug": (C.c_int, [C.c_int]),
     "tsb_add_scaled": (C.c_int, [_p, C.c_int, C.c_int, _p]),
+    "tsb_ep_unique_id": (C.c_int, [_p]),
+    "tsb_ep_create": (C.c_int, [_p, C.c_int, C.c_int, C.POINTER(ExpertLayout), _p, C.c_uint64, C.c_int, C.c_int,
+                                C.c_int, C.c_int, C.c_int, _f, C.POINTER(C.c_void_p)]),
+    "tsb_ep_set_timeout_ns": (C.c_int, [_p, C.c_uint64]),
+    "tsb_ep_dispatch": (C.c_int, [_p, _p, _p, _p, C.c_int, C.c_int, _p]),
+    "tsb_ep_combine": (C.c_int, [_p, _p, C.c_int, _p, _p, C.c_int, C.c_int, _p]),
+    "tsb_ep_stats": (C.c_int, [_p, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]),
+    "tsb_ep_destroy": (C.c_int, [_p]),
     "tsb_moe_layer_tail": (C.c_int, [_p, _p, _p, _p, _p, _f, C.c_int, C.c_int, _f, _p]),
     "tsb_set_wait_limit_ns": (C.c_int, [_u64]),
 }

@@ -4,6 +4,7 @@
 #include "tsb_prefill.cuh"
 #include "tsb_prefill_k.cuh"
 #include "tsb_mmq.cuh"
+#include "tsb_act_layout.cuh"
 #include "../../include/tsb_moe.h"
 
 #include <cuda_runtime.h>
@@ -20,6 +21,9 @@ int decode_set_wait_limit(unsigned long long ns);   // tsb_decode.cu: that trans
 
 // ================================================================================================ host error state
 static thread_local char g_err[512] = "";
+
+// The failure text of this thread's last call that failed in another translation unit of the library (tsb_ep.cu).
+void set_last_error(const char* msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
 
 static int fail(int code, const char* fmt, ...) {
     va_list ap;
@@ -939,26 +943,6 @@ int tsb_moe_dispatch(const int32_t* ids, int n_ent, int K, int n_expert, int32_t
 
 }  // extern "C"
 // ------------------------------------------------------------------------------------ prefill on the tensor cores
-// The activations' tensor-core layout (tsb_mmq_act_bytes): int8 codes [rows][K], then fp32 d [rows][ldS] and
-// d * sum(codes) [rows][ldS], ldS = K / 32 rounded up to 4 (16-byte rows for the scale tiles' TMA), each part on 256 B.
-struct MmqView {
-    int8_t* codes;
-    float* d;
-    float* s;
-    int ldS;
-};
-static int mmq_lds(int64_t K) { return (int) ((K / 32 + 3) / 4 * 4); }
-static uint64_t al256(uint64_t v) { return (v + 255) & ~255ull; }
-static MmqView mmq_view(const void* base, int64_t rows, int64_t K) {
-    MmqView v;
-    v.ldS = mmq_lds(K);
-    uint8_t* b = (uint8_t*) base;
-    v.codes = (int8_t*) b;
-    v.d = (float*) (b + al256((uint64_t) rows * K));
-    v.s = (float*) (b + al256((uint64_t) rows * K) + al256((uint64_t) rows * v.ldS * 4));
-    return v;
-}
-
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1029,7 +1013,7 @@ extern "C" {
 
 uint64_t tsb_mmq_act_bytes(int64_t rows, int64_t K) {
     if (rows < 0 || K <= 0 || K % 32) return 0;
-    return al256((uint64_t) rows * K) + 2 * al256((uint64_t) rows * mmq_lds(K) * 4);
+    return mmq_act_bytes(rows, K);
 }
 
 int tsb_mmq_quantize(const float* x, int64_t ld_x, const int32_t* row_src, int n_rows, int K, void* act, void* stream) {

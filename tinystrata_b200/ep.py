@@ -19,6 +19,8 @@ compute: the tensor-core prefill path on a GPU (gpu_expert_fn), anything with th
 """
 from __future__ import annotations
 
+import ctypes as C
+
 import torch
 import torch.distributed as dist
 
@@ -114,3 +116,72 @@ def gpu_expert_fn(L, blobs, blob_stride: int, act: int, limit: float = float("in
         return acc
 
     return fn
+
+
+class ExpertParallel:
+    """The device path of expert parallelism (libtsb_moe.so's tsb_ep_*): plan, pack, unpack, local experts, partial
+    sums and the ordered gather as kernels, the exchanges as NCCL point-to-point calls on the library's own
+    communicator, one host synchronisation per step (the row counts).  The same placement and per-token result as
+    ep_forward above, which stays the CPU statement of the algorithm (gloo tests).
+
+    Collective: every rank of `group` constructs it (the NCCL id travels through torch.distributed, the plumbing).
+    blobs: this rank's n_expert / G expert blobs in local order (expert e = local l: cyclic e = l * G + rank).
+
+    One step: dispatch(xq, ids, w) queues the exchanges and returns; work the caller queues on the same stream next
+    (the shared expert) runs while the rows travel; combine(out, ...) computes the local experts per micro-batch as
+    their rows arrive and writes out = (out if accumulate) + the partials in rank order + sigmoid(sgate) shared."""
+
+    def __init__(self, L, blobs, blob_stride: int, n_expert: int, n_used: int, act: int, limit: float = float("inf"),
+                 max_tokens: int = 8192, cyclic: bool = True, group=None):
+        from . import _check, lib
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        uid = (C.c_char * 128)()
+        if self.rank == 0:
+            _check(lib().tsb_ep_unique_id(uid), "ep_unique_id")
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        uid = (C.c_char * 128).from_buffer_copy(obj[0])
+        self.L = L
+        self.blobs = blobs                       # held: the library keeps the pointer
+        self.h = C.c_void_p()
+        _check(lib().tsb_ep_create(uid, self.rank, self.world, C.byref(L), C.c_void_p(blobs.data_ptr()), blob_stride,
+                                   n_expert, n_used, int(cyclic), max_tokens, act, limit, C.byref(self.h)),
+               "ep_create")
+
+    def dispatch(self, xq, ids, w, micro_batches: int = 2, stream=None):
+        from . import _check, _stream, lib
+        T = ids.shape[0]
+        _check(lib().tsb_ep_dispatch(self.h, C.c_void_p(xq.data_ptr()) if T else None,
+                                     C.c_void_p(ids.data_ptr()) if T else None, C.c_void_p(w.data_ptr()) if T else None,
+                                     T, micro_batches, _stream(stream)), "ep_dispatch")
+
+    def combine(self, out, accumulate: bool = False, shared=None, sgate=None, sg_stride: int = 1, bf16: bool = False,
+                stream=None):
+        from . import _check, _ptr, _stream, lib
+        _check(lib().tsb_ep_combine(self.h, _ptr(out) if out is not None and out.numel() else None, int(accumulate),
+                                    _ptr(shared), _ptr(sgate), sg_stride, int(bf16), _stream(stream)), "ep_combine")
+        return out
+
+    def set_timeout(self, seconds: float):
+        from . import _check, lib
+        _check(lib().tsb_ep_set_timeout_ns(self.h, int(seconds * 1e9)), "ep_set_timeout_ns")
+
+    def stats(self) -> dict:
+        from . import _check, lib
+        a, b, c = C.c_int64(), C.c_int64(), C.c_int64()
+        _check(lib().tsb_ep_stats(self.h, C.byref(a), C.byref(b), C.byref(c)), "ep_stats")
+        return {"rows_sent": a.value, "rows_received": b.value, "picks": c.value}
+
+    def close(self):
+        from . import _check, lib
+        if self.h:
+            h, self.h = self.h, C.c_void_p()
+            _check(lib().tsb_ep_destroy(h), "ep_destroy")
+
+    def __del__(self):
+        try:
+            if self.h:
+                self.close()
+        except Exception:
+            pass
