@@ -182,24 +182,24 @@ def prefill_ops(T, H, F, FS, K, E):
     return 2.0 * T * (K * 3 * H * F + 3 * H * FS) + 2.0 * T * H * E
 
 
-def bench_prefill(args):
+INT8_SPEC_TOPS = 4500.0   # B200 dense int8 tensor-core rate (NVIDIA's 9 POP/s figure is with 2:4 sparsity)
+
+
+def prefill_measure(lfm: bool, T: int, steps: int, warmup: int, local: int = 0) -> dict:
     """C2: one Gemma-4-26B-A4B-shaped layer (128 Q4_0 experts, top-8, dense Q4_0 shared FFN 2112, GELU-tanh) over
-    T = 8192 prompt tokens; C3 (--workload prefill_lfm): one LFM2.5-24B-A2B-shaped layer (64 experts, top-4 by sigmoid,
-    SwiGLU 1792, Q4_K gate/up, Q6_K down, no shared expert) over T = 2048 with router logits near N(0, 2): router GEMM,
-    routing, q8_1, dispatch, grouped gate/up + down on tcgen05, shared FFN, combine, replayed as one CUDA graph."""
+    T = 8192 prompt tokens; C3 (lfm): one LFM2.5-24B-A2B-shaped layer (64 experts, top-4 by sigmoid, SwiGLU 1792,
+    Q4_K gate/up, Q6_K down, no shared expert) over T = 2048 with router logits near N(0, 2): router GEMM, routing,
+    q8_1, dispatch, grouped gate/up + down on tcgen05, shared FFN, combine, replayed as one CUDA graph."""
     import torch
     import tinystrata_b200 as TS
     from tinystrata_b200 import synth
     from tinystrata_b200.layer import PrefillLayer
 
-    ws, rank, local = dist_env()
-    torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    lfm = args.workload == "prefill_lfm"
     # C3's router logits N(0, 2): weights of sd 2 / sqrt(H) on RMS-normed inputs
     cfg = dict(synth.LFM, router_sd=2.0 / np.sqrt(synth.LFM["n_embd"])) if lfm else synth.GEMMA
     seed = 3 if lfm else 2
-    T, H, F, FS, K, E = args.tokens, cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
+    H, F, FS, K, E = cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
     st = synth.device_layers(cfg, 1, seed=seed, device=device)
     escale = None if lfm else torch.ones(E, dtype=torch.float32, device=device)
     P = PrefillLayer(cfg, st["blobs"][0], st["routers"][0], None if lfm else st["sh_blobs"][0], max_tokens=T,
@@ -237,44 +237,85 @@ def bench_prefill(args):
         stream.synchronize()
         return e0.elapsed_time(e1) / n
 
-    timed(g, max(3, args.warmup))
+    timed(g, max(3, warmup))
     with Clocks(local) as clk:
-        ms = timed(g, args.steps)
-    ms_e2e = timed(ge, max(3, args.steps // 2))
+        ms = timed(g, steps)
+    ms_e2e = timed(ge, max(3, steps // 2))
+    # the grouped gate/up kernel alone (the dominant kernel), CUDA events on its stream
+    n = T * K
+    with torch.cuda.stream(stream):
+        kev = []
+        for _ in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            TS.moe_prefill_gu(P.L, P.blobs, P.stride, P.bounds, E, n, P.xa, cfg["act"], h=P.ha, stream=stream)
+            b.record(stream)
+            kev.append((a, b))
+    stream.synchronize()
+    gu_ms = float(np.mean([a.elapsed_time(b) for a, b in kev[1:]]))
     assert TS.device_error() == 0
     ops = prefill_ops(T, H, F, FS, K, E)
-    peak = 1647.6
+    gu_ops = 2.0 * n * 2 * H * F
+    bf16_peak = None
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            peak = float(json.load(f)["bf16_tflops"])
-        peak_kind = "measured bf16 dense (the fp16 tensor-core rate)"
+            bf16_peak = float(json.load(f)["bf16_tflops"])
     except (OSError, KeyError, ValueError):
-        peak_kind = "fallback"
+        pass
     achieved = ops / (ms * 1e-3) / 1e12
     wbytes = int(st["blobs"][0].numel())
-    line = {
+    del g, ge
+    return {
         "metric": PREFILL_LFM_METRIC if lfm else PREFILL_METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s",
-        "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "n_gpus": 1, "ms_per_step": ms, "us_per_layer": ms * 1e3,
         "dtype": ("q8_1 x " + ("Q4_K / Q6_K" if lfm else "Q4_0") +
-                  " exact integer block dots on tcgen05 (fp16 operands holding integers), fp32 block scaling"),
-        "data": "synthetic",
+                  " exact int32 block sums on tcgen05.mma.kind::i8 (TMA-staged activations), fp32 block scaling"),
         "config": {"workload": f"prefill T={T} through one " +
                                ("LFM2.5-24B-A2B" if lfm else "Gemma-4-26B-A4B") + "-shaped MoE layer",
                    "tokens": T, "hidden": H, "experts": E, "top_k": K, "n_ff": F, "shared_n_ff": FS,
                    "weights": "Q4_K gate/up, Q6_K down" if lfm else "Q4_0",
                    "l2": f"expert weights {wbytes / 1e6:.0f} MB (" +
                          ("larger" if wbytes > 126e6 else "smaller") + " than L2); no flush between steps"},
-        "us_per_layer": ms * 1e3,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s (int8-op/s, algorithmic)",
-                     "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+        "roofline": {"bound": "tensor", "kernel": "k_mmq<gate/up> (grouped gate/up + activation, the top kernel)",
+                     "achieved": gu_ops / (gu_ms * 1e-3) / 1e12, "peak": INT8_SPEC_TOPS,
+                     "unit": "TOP/s (int8, algorithmic)", "frac": gu_ops / (gu_ms * 1e-3) / 1e12 / INT8_SPEC_TOPS,
+                     "peak_kind": "B200 dense int8 spec (4.5 POP/s; no measured int8 peak on this pool)",
+                     "traffic": None, "avg_launch_ms": gu_ms, "algorithmic_ops_per_launch": gu_ops,
+                     "layer_achieved": achieved, "layer_frac": achieved / INT8_SPEC_TOPS,
+                     "layer_frac_of_measured_bf16": achieved / bf16_peak if bf16_peak else None,
                      "algorithmic_ops_per_layer": ops},
         "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
                 "h2d_bytes_per_step": int(x0_host.numel() * 4), "d2h_bytes_per_step": int(out_host.numel() * 4)},
-        "clocks": clk.summary(), "cpu_baseline": None,
+        "gpu_launches_per_step": 11 if not lfm else 8,
+        "clocks": clk.summary(),
     }
+
+
+def prefill_cpu_baseline(lfm: bool) -> dict | None:
+    """C2's routed experts through a C restatement of the reference's CPU expert path (gemma4/cpu_experts.cpp:145-235,
+    oracle/cpu_experts_port.c) on this host's cores, for about 10 s (None for C3, which has no CPU port)."""
+    if lfm:
+        return None
+    try:
+        from oracle import oracle as O
+        from tinystrata_b200 import synth
+        return O.cpu_baseline_prefill(synth.GEMMA, seconds=10.0)
+    except Exception as e:  # the baseline is reported, never required
+        return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "port", "sample": f"unavailable: {e}"}
+
+
+def bench_prefill(args):
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    lfm = args.workload == "prefill_lfm"
+    r = prefill_measure(lfm, args.tokens, args.steps, args.warmup, local)
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = prefill_cpu_baseline(lfm)
+    line = dict(r, steps=args.steps, warmup=args.warmup, higher_is_better=True, scaling="weak", vs_baseline=None,
+                data="synthetic", cpu_baseline=cpu, gpu_launches=r["gpu_launches_per_step"] * args.steps)
     print(json.dumps(line), flush=True)
-    del g, ge
     return 0
 
 
@@ -282,32 +323,35 @@ EP_METRIC = "EP prefill MoE-layer tokens/s (Gemma-4-26B-A4B-shaped Q4_0 layer, T
 EPQ_METRIC = "EP prefill MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped IQ3_XXS/IQ3_S layer, T=65536, experts sharded)"
 
 
-def bench_ep_qwen(args):
+def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16: bool = True,
+                    own_group: bool = True) -> dict | None:
     """C4: the Qwen3.6-35B-A3B-shaped layer (256 experts, IQ3_XXS gate/up, IQ3_S down, top-8 softmax, Q8_0 shared
     expert gated by a sigmoid of the 257th router row) over T = 65536 prompt tokens split evenly over the ranks
     (strong scaling), experts sharded 256 / N per GPU in cyclic placement (expert e on rank e % N: the skewed head
     spreads over the ranks), router logits skewed by a Zipf(1.1) prior over the experts (log p_e added to expert
-    e's logit) so that the expert load is imbalanced.  Per step: router GEMM, routing, q8_1,
-    dispatch / return all-to-alls over NCCL, local experts and the shared expert on the tensor cores, gated sum.
-    Eager (host-synchronising counts), timed with CUDA events between barriers, max over ranks."""
+    e's logit) so that the expert load is imbalanced.  Per step: router GEMM, routing, q8_1, the device expert-parallel
+    path (tsb_ep_dispatch: plan, pack, counts exchange -- the step's one host synchronisation -- and the micro-batched
+    dispatch exchanges over NCCL; the shared expert on a second stream meanwhile; tsb_ep_combine: local experts on the
+    tensor cores per micro-batch, partial rows back, the rank-ordered gated sum).  Timed with CUDA events between
+    barriers, max over ranks.  Returns rank 0's result (None on the other ranks)."""
     import datetime
     import torch
     import torch.distributed as dist
     import tinystrata_b200 as TS
     from tinystrata_b200 import synth
-    from tinystrata_b200.ep import ep_forward, gpu_expert_fn
+    from tinystrata_b200.ep import ExpertParallel
 
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if ws > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    else:
-        import tempfile
-        dist.init_process_group("nccl", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1,
-                                device_id=device)
+    if own_group:
+        if ws > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        else:
+            import tempfile
+            dist.init_process_group("gloo", init_method="file://" + tempfile.mktemp(), rank=0, world_size=1)
     cfg = synth.QWEN_EP
-    T_all = args.tokens if args.tokens > 1 else 65536
+    T_all = 65536
     T = T_all // ws
     H, F, FS, K, E = cfg["n_embd"], cfg["n_ff"], cfg["sh_n_ff"], cfg["n_used"], cfg["n_expert"]
     per = E // ws
@@ -318,55 +362,109 @@ def bench_ep_qwen(args):
     L = TS.native_expert_layout(cfg["gu_type"], cfg["d_type"], H, F)
     Ls = TS.native_expert_layout(cfg["sh_gu_type"], cfg["sh_d_type"], H, FS)
     zipf = torch.tensor(-1.1 * np.log(np.arange(1, E + 1)), dtype=torch.float32, device=device)
-    x0 = torch.from_numpy(synth.rms_normed(np.random.default_rng(4 + rank), T, H)).to(device)
-    fn = gpu_expert_fn(L, blobs, int(L.bytes), cfg["act"])
+    x0_np = synth.rms_normed(np.random.default_rng(4 + rank), T, H)
+    x0 = torch.from_numpy(x0_np).to(device)
+    ep = ExpertParallel(L, blobs, int(L.bytes), E, K, cfg["act"], max_tokens=T, cyclic=True)
+    logits = torch.empty((T, E + 1), dtype=torch.float32, device=device)
+    ids = torch.empty((T, K), dtype=torch.int32, device=device)
+    w = torch.empty((T, K), dtype=torch.float32, device=device)
+    xq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
+    xs = TS.MmqAct(T, H, device)
+    hs = TS.MmqAct(T, FS, device)
+    shared = torch.empty((T, H), dtype=torch.float32, device=device)
+    out = torch.empty((T, H), dtype=torch.float32, device=device)
+    main = torch.cuda.current_stream(device)
+    side = torch.cuda.Stream(device)
 
-    def step():
-        logits = TS.router_logits_f32(router, x0)                 # [T, E + 1]: the experts, then the shared gate
-        lg = logits[:, :E] + zipf
-        ids, w = TS.native_router_topk(lg.contiguous(), K)       # softmax top-8, renormalised (the Qwen router)
-        xq = TS.quantize_q8_1_rows(x0)
-        out = ep_forward(xq, ids, w, E, H, fn, cyclic=True)
-        hs = TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, TS.mmq_quantize(x0), cfg["act"])
-        shared = TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs)
-        return out.addcmul_(shared, torch.sigmoid(logits[:, E:E + 1]))
+    def step(x):
+        TS.router_logits_f32(router, x, logits, ld=E + 1)       # [T, E + 1]: the experts, then the shared gate
+        logits[:, :E].add_(zipf)
+        TS.native_router_topk(logits, K, E, ids, w)             # softmax top-8, renormalised (the Qwen router)
+        TS.quantize_q8_1_rows(x, xq)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        side.wait_event(ready)
+        with torch.cuda.stream(side):                            # the shared expert while the rows travel
+            TS.mmq_quantize(x, out=xs, stream=side)
+            TS.moe_prefill_gu(Ls, sh, 0, None, 1, T, xs, cfg["act"], h=hs, stream=side)
+            TS.moe_prefill_down(Ls, sh, 0, None, 1, T, hs, out=shared, stream=side)
+        done = torch.cuda.Event()
+        done.record(side)
+        ep.dispatch(xq, ids, w, micro_batches=micro_batches)
+        main.wait_event(done)
+        ep.combine(out, accumulate=False, shared=shared, sgate=logits[:, E:], sg_stride=E + 1, bf16=bf16)
+        return out
 
-    for _ in range(max(3, args.warmup)):
-        step()
+    for _ in range(max(3, warmup)):
+        step(x0)
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
+        e0.record(main)
+        for _ in range(steps):
+            step(x0)
+        e1.record(main)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = e0.elapsed_time(e1) / steps
+    # end to end: the step's tokens from pinned host memory, the layer output back, every step
+    x_host = torch.from_numpy(x0_np).pin_memory()
+    o_host = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    xin = torch.empty_like(x0)
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(main)
+    for _ in range(max(2, steps // 2)):
+        xin.copy_(x_host, non_blocking=True)
+        step(xin)
+        o_host.copy_(out, non_blocking=True)
+    b.record(main)
+    torch.cuda.synchronize()
+    ms_e2e = a.elapsed_time(b) / max(2, steps // 2)
+    stats = ep.stats()
+    t = torch.tensor([ms, ms_e2e, float(stats["picks"])], device=device)
+    if ws > 1:
+        dist.all_reduce(t[:2], op=dist.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+    ep.close()
     assert TS.device_error() == 0
+    res = None
     if rank == 0:
         ops = prefill_ops(T_all, H, F, FS, K, E + 1)
-        line = {
+        res = {
             "metric": EPQ_METRIC, "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "q8_1 x IQ3_XXS / IQ3_S / Q8_0 exact integer block dots on tcgen05, fp32 block scaling",
             "data": "synthetic (Zipf(1.1)-skewed router logits)",
             "config": {"workload": f"expert-parallel prefill, {T_all} tokens over {ws} GPU(s), {per} of {E} "
                                    "experts per GPU", "tokens": T_all, "tokens_per_gpu": T, "experts_per_gpu": per,
-                       "placement": "cyclic (expert e on rank e % N)",
-                       "parallelism": f"ep{ws}",
-                       "collectives": "NCCL all_to_all_single (counts, q8_1 rows, picks; fp32 partial rows back)"},
+                       "placement": "cyclic (expert e on rank e % N)", "parallelism": f"ep{ws}",
+                       "micro_batches": micro_batches, "return": "bf16" if bf16 else "fp32",
+                       "collectives": "NCCL send/recv on the library's communicator (counts; q8_1 rows, local "
+                                      "picks, weights; partial rows back), one host synchronisation per step"},
             "us_per_layer": ms * 1e3,
-            "roofline": {"bound": "tensor", "achieved": ops / (ms * 1e-3) / 1e12 / ws, "unit": "TFLOP/s per GPU",
+            "rank0_rows": stats,
+            "roofline": {"bound": "tensor", "achieved": ops / (ms * 1e-3) / 1e12 / ws, "unit": "TOP/s per GPU",
+                         "peak": INT8_SPEC_TOPS, "frac": ops / (ms * 1e-3) / 1e12 / ws / INT8_SPEC_TOPS,
+                         "peak_kind": "B200 dense int8 spec (4.5 POP/s); no measured int8 peak",
                          "note": "int8-op/s, algorithmic"},
+            "e2e": {"value": T_all / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": int(x_host.numel() * 4) * ws,
+                    "d2h_bytes_per_step": int(o_host.numel() * 4) * ws},
             "clocks": clk.summary(),
         }
-        print(json.dumps(line), flush=True)
-    dist.destroy_process_group()
+    if own_group:
+        dist.destroy_process_group()
+    return res
+
+
+def bench_ep_qwen(args):
+    res = ep_qwen_measure(args, args.steps, args.warmup)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
 
 
 def bench_ep(args):

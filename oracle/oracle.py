@@ -380,3 +380,69 @@ def cpu_baseline_decode(cfg: dict, seconds: float = 10.0, threads: int | None = 
             "sample": f"{done} decode tokens x 1 layer ({cfg['name']}, {K} routed experts each of {E} resident in host "
                       f"memory, reference iq512/iq256 rows + q8k_quant_avx2, {threads} worker threads), "
                       f"{elapsed:.1f} s"}
+
+
+_CX = None
+
+
+def cx_port():
+    """oracle/libcx_port.so: the C restatement of the reference's CPU expert path (cpu_experts_port.c)."""
+    global _CX
+    with _lock:
+        if _CX is None:
+            path = os.path.join(HERE, "libcx_port.so")
+            if not os.path.exists(path):
+                build(ref=False)
+            L = C.CDLL(path)
+            L.cx_moe_experts_q4_0.restype = C.c_int
+            L.cx_moe_experts_q4_0.argtypes = [_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, C.c_int, _p, C.c_int,
+                                              _p, _p, C.c_int, C.c_int, _f, C.c_int, _p]
+            _CX = L
+    return _CX
+
+
+def cx_moe_experts_q4_0(blobs, layout: dict, n_embd: int, n_ff: int, x, ids, w, gelu: bool, limit=float("inf"),
+                        threads: int = 1):
+    """The routed experts of `x` (fp32 [rows, n_embd]) through cpu_experts_port.c: fp32 [rows, n_embd]."""
+    blobs = np.ascontiguousarray(blobs)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, K = ids.shape
+    out = np.zeros((rows, n_embd), np.float32)
+    rc = cx_port().cx_moe_experts_q4_0(_ptr(blobs), blobs.shape[1], layout["up_off"], layout["down_off"], n_embd,
+                                       n_ff, _ptr(x), rows, _ptr(ids), _ptr(w), K, int(gelu), limit, threads,
+                                       _ptr(out))
+    if rc != 0:
+        raise ValueError("cx_moe_experts_q4_0: arguments")
+    return out
+
+
+def cpu_baseline_prefill(cfg: dict, seconds: float = 10.0, threads: int | None = None, seed: int = 2,
+                         chunk: int = 256) -> dict:
+    """C2's routed experts (Q4_0 Gemma-4-shaped layer, every expert in host memory, uniform routing) through the C
+    restatement of the reference's CPU expert path (cpu_experts_port.c, gemma4/cpu_experts.cpp:145-235) on this host's
+    cores, prompt chunks of `chunk` tokens for about `seconds`: tokens/s through the layer's routed experts."""
+    import time
+    from tinystrata_b200 import synth
+    threads = threads or physical_cores()
+    layer = synth.make_layer(cfg, seed)
+    blobs = np.ascontiguousarray(layer["blobs"])
+    E, K, H, F = cfg["n_expert"], cfg["n_used"], cfg["n_embd"], cfg["n_ff"]
+    L = synth.blob_layout(cfg)
+    rng = np.random.default_rng(seed)
+    done, elapsed = 0, 0.0
+    t_end = time.time() + seconds
+    while time.time() < t_end or done < chunk:
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(chunk)]).astype(np.int32)
+        w = rng.dirichlet(np.ones(K), size=chunk).astype(np.float32)
+        x = synth.rms_normed(rng, chunk, H)
+        t0 = time.perf_counter()
+        cx_moe_experts_q4_0(blobs, L, H, F, x, ids, w, gelu=True, threads=threads)
+        elapsed += time.perf_counter() - t0
+        done += chunk
+    return {"value": done / elapsed, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{done} prompt tokens in chunks of {chunk} x 1 layer ({cfg['name']}, {K} of {E} Q4_0 routed "
+                      f"experts resident in host memory; shared FFN, router and combine not included), C restatement "
+                      f"of gemma4/cpu_experts.cpp:145-235 with ggml's Q4_0 x Q8_0 dot, {threads} worker threads, "
+                      f"{elapsed:.1f} s"}

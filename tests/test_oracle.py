@@ -216,3 +216,25 @@ def test_layer_oracle_small():
     ref = out["parts"][t, k].astype(np.float64)
     rel = np.linalg.norm(ref - y) / np.linalg.norm(y)
     assert rel < 2e-2, rel   # q8_1 of the hidden layer and IQ3_XXS's integer truncation against exact float math
+
+
+def test_cpu_port_of_reference_experts_matches_oracle():
+    """cpu_experts_port.c (the C2 CPU baseline: the reference's cpu_experts task structure with ggml's Q4_0 x Q8_0
+    dot restated) against the oracle's experts on the same tokens: the two quantise activations differently (q8_0 vs
+    q8_1 scales are the same, the rounding of x / d differs only at ties), so a layer tolerance."""
+    from tinystrata_b200 import synth
+    cfg = dict(synth.GEMMA, n_expert=8)
+    layer = synth.make_layer(cfg, 5)
+    rng = np.random.default_rng(5)
+    H, F, K = cfg["n_embd"], cfg["n_ff"], cfg["n_used"]
+    x = synth.rms_normed(rng, 3, H)
+    ids = np.stack([rng.choice(8, K, replace=False) for _ in range(3)]).astype(np.int32)
+    w = rng.random((3, K)).astype(np.float32)
+    got = O.cx_moe_experts_q4_0(layer["blobs"], synth.blob_layout(cfg), H, F, x, ids, w, gelu=True, threads=4)
+    parts = O.experts_for_tokens(cfg["gu_type"], cfg["d_type"], layer["blobs"], H, F, O.quantize_q8_1(x), ids,
+                                 cfg["act"])
+    ref = O.combine(None, parts, w)
+    m, r = got.astype(np.float64).ravel(), np.asarray(ref, np.float64).ravel()
+    err = np.abs(m - r).max() / np.sqrt(np.mean(r ** 2))
+    cos = m @ r / (np.linalg.norm(m) * np.linalg.norm(r))
+    assert err <= 2e-2 and cos >= 0.9999, (err, cos)

@@ -133,14 +133,14 @@ __device__ __forceinline__ void tmem_fill32(uint32_t addr, uint32_t v) {
                      : "memory");
 }
 // Two columns at once: a += w * (fma(f, dx, ndxm)) with the packed fp32 pipe instructions (the same IEEE roundings as
-// two scalar fma pairs, half the instructions).
+// two scalar fma pairs, half the instructions).  The intrinsic, not inline assembly: the compiler schedules it.
 __device__ __forceinline__ void mq_fma2(float& a0, float& a1, float w0, float w1, uint32_t f0, uint32_t f1, float dx,
                                         float ndxm) {
-    asm volatile("{\n .reg .b64 f, x, m, t, w, a;\n mov.b64 f, {%2, %3};\n mov.b64 x, {%4, %4};\n mov.b64 m, {%5, %5};\n"
-        " fma.rn.f32x2 t, f, x, m;\n mov.b64 w, {%6, %7};\n mov.b64 a, {%0, %1};\n fma.rn.f32x2 a, w, t, a;\n"
-        " mov.b64 {%0, %1}, a;\n}\n"
-        : "+f"(a0), "+f"(a1)
-        : "r"(f0), "r"(f1), "f"(dx), "f"(ndxm), "f"(w0), "f"(w1));
+    const float2 t = __ffma2_rn(make_float2(__uint_as_float(f0), __uint_as_float(f1)), make_float2(dx, dx),
+                                make_float2(ndxm, ndxm));
+    const float2 r = __ffma2_rn(make_float2(w0, w1), t, make_float2(a0, a1));
+    a0 = r.x;
+    a1 = r.y;
 }
 // Four weight terms from shared memory, in program order with the FMAs that use them (volatile: the compiler may not
 // hoist all sixteen of a block's loads ahead of its FMAs, which would need 64 more registers than a thread has).
@@ -151,10 +151,9 @@ __device__ __forceinline__ float4 lds4(const float4* p) {
 }
 // a += w * t for two columns, t given (packed).
 __device__ __forceinline__ void mq_fma2t(float& a0, float& a1, float w0, float w1, float t0, float t1) {
-    asm volatile("{\n .reg .b64 t, w, a;\n mov.b64 t, {%2, %3};\n mov.b64 w, {%4, %5};\n mov.b64 a, {%0, %1};\n"
-        " fma.rn.f32x2 a, w, t, a;\n mov.b64 {%0, %1}, a;\n}\n"
-        : "+f"(a0), "+f"(a1)
-        : "f"(t0), "f"(t1), "f"(w0), "f"(w1));
+    const float2 r = __ffma2_rn(make_float2(w0, w1), make_float2(t0, t1), make_float2(a0, a1));
+    a0 = r.x;
+    a1 = r.y;
 }
 
 // Four int8 values b - 8 from four nibbles b (one per byte): (b + 0x78) ^ 0x80 per byte, with no carry between bytes.
