@@ -7,6 +7,11 @@ GEMVs + shared expert + gated combine + the next layer's RMS/q8_1), replayed as 
 MoE-layer tokens/s (T / mean layer time) with microseconds per layer beside it.  Decode does not shard: with --gpus N
 each rank runs its own replica (weak scaling) and `value` sums the replicas.
 
+The same line carries the other configurations as keys: decode_sweep (T = 2, 4, 16), prefill_c2 (Gemma-4-shaped Q4_0
+layer, T = 8192) and prefill_c3 (LFM2.5-shaped Q4_K / Q6_K layer, T = 2048) on one GPU, each with its CPU baseline
+where one exists, and ep_c4 (the Qwen IQ3 layer over T = 65536 tokens, experts sharded over every rank of the run).
+--workload selects one of them alone.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl tsb|reference]
 """
 from __future__ import annotations
@@ -555,6 +560,8 @@ def main():
     ap.add_argument("--impl", default="tsb", choices=["tsb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sweep", action="store_true", help="only the headline token count (profiling captures)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode only: without the C2 / C3 prefill and C4 expert-parallel keys")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen"],
@@ -755,6 +762,22 @@ def bench_decode(args):
         except Exception as e:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
+    # the other headline configurations as extra keys: C2 / C3 prefill (one GPU) and C4 expert-parallel prefill
+    # (every rank of the run, the sharded configuration)
+    extras = {}
+    if not args.no_extras:
+        if ws == 1:
+            for key, lfm, T_p in (("prefill_c2", False, 8192), ("prefill_c3", True, 2048)):
+                r = prefill_measure(lfm, T_p, 10, 3, local)
+                r["cpu_baseline"] = None if args.no_cpu_baseline else prefill_cpu_baseline(lfm)
+                extras[key] = {k: r[k] for k in ("metric", "value", "unit", "us_per_layer", "ms_per_step", "dtype",
+                                                 "config", "roofline", "e2e", "clocks", "cpu_baseline")}
+                extras[key]["gpu_launches"] = r["gpu_launches_per_step"] * 10
+        r = ep_qwen_measure(args, 5, 3, own_group=(ws == 1))
+        if r is not None:
+            extras["ep_c4"] = {k: r[k] for k in ("metric", "value", "unit", "n_gpus", "us_per_layer", "ms_per_step",
+                                                 "scaling", "config", "roofline", "e2e", "clocks", "rank0_rows")}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": head["tokens_per_s"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
@@ -777,6 +800,7 @@ def bench_decode(args):
             "clocks": head["clocks"],
             "cpu_baseline": cpu,
             "decode_sweep": sweep,
+            **extras,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
