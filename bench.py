@@ -402,6 +402,7 @@ def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16:
 
     for _ in range(max(3, warmup)):
         step(x0)
+    ep.synchronize()
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -410,6 +411,7 @@ def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16:
         for _ in range(steps):
             step(x0)
         e1.record(main)
+        ep.synchronize()   # bounded: a peer that stops answering ends the run with an error, not a hang
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     # end to end: the step's tokens from pinned host memory, the layer output back, every step
@@ -425,6 +427,7 @@ def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16:
         step(xin)
         o_host.copy_(out, non_blocking=True)
     b.record(main)
+    ep.synchronize()
     torch.cuda.synchronize()
     ms_e2e = a.elapsed_time(b) / max(2, steps // 2)
     stats = ep.stats()

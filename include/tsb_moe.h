@@ -266,6 +266,7 @@ int tsb_ep_create(const void* id128, int rank, int world, const tsb_expert_layou
  * shared expert) before tsb_ep_combine. */
 int tsb_ep_dispatch(tsb_ep* ep, const void* x_q8_1, const int32_t* ids, const float* w, int n_tok, int micro_batches,
                     void* stream);
+/* micro_batches is collective: every rank passes the same value (a rank's slice may hold no tokens). */
 /* Finish the step tsb_ep_dispatch started: per micro-batch the local grouped experts on the tensor cores as its rows
  * arrive, the weighted partial row per received token, its return exchange; then per token, on `stream`,
  * out = (accumulate ? out : 0) + the partials of the ranks it went to in rank order (+ sigmoid(sgate[t * sg_stride])
@@ -275,6 +276,9 @@ int tsb_ep_combine(tsb_ep* ep, float* out, int accumulate, const float* shared, 
 /* The bound of the host's waits on the exchanges (default 120 s): past it the communicator is aborted and the call
  * returns TSB_ERR_COMM (the handle is then only good for tsb_ep_destroy). */
 int tsb_ep_set_timeout_ns(tsb_ep* ep, uint64_t ns);
+/* Wait, within the bound, for every exchange issued so far (host-synchronous; a caller that reads results on the host
+ * calls it before synchronising its own stream, so that a peer that never answers ends in TSB_ERR_COMM). */
+int tsb_ep_synchronize(tsb_ep* ep);
 /* The last step's rows: rows sent to other ranks and to this one, rows received, picks computed here. */
 int tsb_ep_stats(const tsb_ep* ep, int64_t* sent, int64_t* received, int64_t* picks);
 /* Free the buffers and the communicator (collective). */

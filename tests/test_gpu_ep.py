@@ -104,8 +104,7 @@ def _ep_worker(rank, world, port, q, scenario):
         mine = torch.from_numpy(layer["blobs"][rank::world].copy()).to(dev)   # cyclic placement
         sh = torch.from_numpy(layer["sh_blob"]).to(dev)
         ep = ExpertParallel(L, mine, int(L.bytes), E, K, cfg["act"], max_tokens=160, cyclic=True)
-        if scenario == "timeout":
-            ep.set_timeout(3.0)
+        ep.set_timeout(3.0 if scenario == "timeout" else 60.0)
         results = []
         steps = [(1, False, 100), (2, False, 100), (3, True, 100), (2, False, 0 if rank == 1 else 37)]
         if scenario == "timeout":
@@ -134,6 +133,7 @@ def _ep_worker(rank, world, port, q, scenario):
                 shared = T.moe_prefill_down(Ls, sh, 0, None, 1, T_tok, hs)
             sgd = torch.from_numpy(sg).to(dev)
             ep.combine(out, accumulate=False, shared=shared, sgate=sgd if T_tok else None, bf16=bf16)
+            ep.synchronize()           # bounded: a peer that never answers ends here with an error
             torch.cuda.synchronize()
             st = ep.stats()
             if T_tok == 0:

@@ -94,6 +94,7 @@ SIGNATURES = {
     "tsb_ep_dispatch": (C.c_int, [_p, _p, _p, _p, C.c_int, C.c_int, _p]),
     "tsb_ep_combine": (C.c_int, [_p, _p, C.c_int, _p, _p, C.c_int, C.c_int, _p]),
     "tsb_ep_stats": (C.c_int, [_p, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]),
+    "tsb_ep_synchronize": (C.c_int, [_p]),
     "tsb_ep_destroy": (C.c_int, [_p]),
     "tsb_moe_layer_tail": (C.c_int, [_p, _p, _p, _p, _p, _f, C.c_int, C.c_int, _f, _p]),
     "tsb_set_wait_limit_ns": (C.c_int, [_u64]),

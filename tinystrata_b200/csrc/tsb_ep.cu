@@ -457,6 +457,7 @@ int tsb_ep_create(const void* id128, int rank, int world, const tsb_expert_layou
         return efail(TSB_ERR_ARG, "ep_create: arguments (1..%d ranks, experts a multiple of the ranks, 1..32 picks)",
                      kEpMaxWorld);
     if (L->n_embd % 128) return efail(TSB_ERR_UNSUPPORTED, "ep_create: n_embd a multiple of 128");
+    if (n_expert / world > 512) return efail(TSB_ERR_UNSUPPORTED, "ep_create: at most 512 experts per rank");
     const Nccl* N = nccl_lib();
     if (!N) return efail(TSB_ERR_COMM, "ep_create: libnccl.so.2 could not be loaded");
     tsb_ep* ep = new tsb_ep();
@@ -474,7 +475,7 @@ int tsb_ep_create(const void* id128, int rank, int world, const tsb_expert_layou
     ep->stride = blob_stride;
     ep->H = (int) L->n_embd;
     ep->RB = ep->H / 32 * 36;
-    ep->kloc = n_used < ep->per ? n_used : ep->per;
+    ep->kloc = n_used;   // a row's picks on one rank: up to all of them (a token may pick an expert twice)
     ep->S_cap = (int64_t) max_tokens * (n_used < world ? n_used : world);
     ep->R_cap = (int64_t) max_tokens * world;
     ep->P_cap = ep->R_cap * ep->kloc;
@@ -544,7 +545,9 @@ int tsb_ep_dispatch(tsb_ep* ep, const void* x_q8_1, const int32_t* ids, const fl
         return efail(TSB_ERR_ARG, "ep_dispatch: arguments (0..%d tokens, 1..%d micro-batches)", ep->max_tok, kEpMaxMb);
     if ((uintptr_t) x_q8_1 % 16) return efail(TSB_ERR_ALIGN, "ep_dispatch: q8_1 rows 16-byte aligned");
     cudaStream_t s = (cudaStream_t) stream;
-    const int G = ep->world, M = n_tok >= micro_batches ? micro_batches : (n_tok > 0 ? n_tok : 1), K = ep->K;
+    // every rank exchanges M counts with every peer: M is the caller's (the same on every rank), never derived from
+    // this rank's token count (a slice may hold no tokens)
+    const int G = ep->world, M = micro_batches, K = ep->K;
     if (n_tok > 0) {
         k_ep_plan<<<1, 1024, 0, s>>>(ids, n_tok, K, ep->E, G, ep->per, ep->cyclic, M, ep->send_pos, ep->counts);
         k_ep_pack<<<(unsigned) ((n_tok + 7) / 8), 256, 0, s>>>((const uint8_t*) x_q8_1, ep->RB, ids, w, n_tok, K, ep->E,
@@ -696,6 +699,13 @@ int tsb_ep_combine(tsb_ep* ep, float* out, int accumulate, const float* shared, 
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return efail(TSB_ERR_CUDA, "ep_combine: %s", cudaGetErrorString(e));
     return TSB_OK;
+}
+
+int tsb_ep_synchronize(tsb_ep* ep) {
+    if (!ep) return efail(TSB_ERR_ARG, "ep_synchronize: null handle");
+    if (ep->broken) return efail(TSB_ERR_COMM, "ep_synchronize: the communicator was aborted");
+    cudaEventRecord(ep->ev_counts, ep->cs);
+    return ep_wait(ep, ep->ev_counts, "synchronize");
 }
 
 int tsb_ep_stats(const tsb_ep* ep, int64_t* sent, int64_t* received, int64_t* picks) {

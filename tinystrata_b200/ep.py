@@ -163,6 +163,11 @@ class ExpertParallel:
                                     _ptr(shared), _ptr(sgate), sg_stride, int(bf16), _stream(stream)), "ep_combine")
         return out
 
+    def synchronize(self):
+        """Wait (bounded) for every exchange issued so far; TsbError (status -6) when a peer never answers."""
+        from . import _check, lib
+        _check(lib().tsb_ep_synchronize(self.h), "ep_synchronize")
+
     def set_timeout(self, seconds: float):
         from . import _check, lib
         _check(lib().tsb_ep_set_timeout_ns(self.h, int(seconds * 1e9)), "ep_set_timeout_ns")
