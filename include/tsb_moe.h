@@ -161,6 +161,15 @@ int tsb_moe_prefill_gu(const tsb_expert_layout* L, const void* blobs, uint64_t b
  * h_act the hidden rows tsb_moe_prefill_gu wrote.  Replaces the down mmq::Context::run (src/prefill/moe_mmq.cu:334-384). */
 int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t blob_stride, const int32_t* bounds,
                          int n_groups, int n_rows, const void* h_act, float* out, void* stream);
+/* A grouped product on the tensor cores with fp32 output: for each of n matrices of [w_rows][w_cols] weights of
+ * ggml_type, `stride` bytes apart from w, the activation rows [bounds[e], bounds[e+1]) of x_act (the tensor-core layout
+ * of total_rows rows of w_cols values) times matrix e; row i's product goes to row ids[i] of dst (row i when ids is
+ * null), ld_dst floats a row.  With one matrix, bounds may be null (every row).  Replaces mmq::Context::run
+ * (include/strata/prefill/moe_mmq.hpp:69-98, src/prefill/moe_mmq.cu) and gemma4::Mmq::mul (src/gemma4/mmq.hpp:36-41,
+ * mmq.cu:74-110). */
+int tsb_mmq_product(const void* w, int ggml_type, int64_t w_rows, int64_t w_cols, uint64_t stride, int n,
+                    const void* x_act, const int32_t* bounds, const int32_t* ids, int64_t total_rows, float* dst,
+                    int64_t ld_dst, void* stream);
 
 /* Bench only: 0 = both expert kernels (default), 1 = gate/up + activation only, 2 = down only (reads the scratch the
  * previous call left).  Replaces native_expert_set_mode's phase argument (iq_kernels.hpp:85).  Process-wide; set

@@ -235,3 +235,37 @@ def test_prefill_layer_gemma_vs_oracle(cuda):
     assert np.array_equal(P.ids.cpu().numpy(), ref["ids"])
     err, cos = tol(xd.cpu().numpy(), ref["out"])
     assert err <= 1e-2 and cos >= 0.9999, (err, cos)
+
+
+@pytest.mark.parametrize("t,w_rows,w_cols", [(synth.T_Q4_0, 192, 2816), (synth.T_IQ3_S, 256, 512),
+                                             (synth.T_Q6_K, 128, 1792)])
+def test_mmq_product_groups_row_map_and_stride(cuda, t, w_rows, w_cols):
+    """tsb_mmq_product (mmq::Context::run / gemma4::Mmq::mul): three matrices over their row ranges, each row's
+    product scattered to dst row ids[i] of a wider dst (ld_dst > w_rows), against fp64 of the dequantised weights and
+    the activation values (codes x d) the kernel read."""
+    rng = np.random.default_rng(90 + t)
+    n, rows = 3, 300
+    rb = synth.row_bytes(t, w_cols)
+    mats = [synth.gen_matrix(rng, t, w_rows, w_cols, 0.02).reshape(w_rows, rb) for _ in range(n)]
+    stride = (w_rows * rb + 255) // 256 * 256
+    wbuf = np.zeros(n * stride, np.uint8)
+    for e in range(n):
+        wbuf[e * stride:e * stride + w_rows * rb] = mats[e].ravel()
+    bounds = np.array([0, 70, 70 + 161, rows], np.int32)
+    ids = rng.permutation(rows).astype(np.int32)
+    x = rng.normal(0, 1, size=(rows, w_cols)).astype(np.float32)
+    xa = T.mmq_quantize(dev(x))
+    ld = w_rows + 36
+    dst = torch.full((rows, ld), float("nan"), device="cuda")
+    T.mmq_product(dev(wbuf), t, w_rows, w_cols, stride, n, xa, bounds=dev(bounds), ids=dev(ids), dst=dst, ld_dst=ld)
+    torch.cuda.synchronize()
+    assert T.device_error() == 0
+    got = dst.cpu().numpy()
+    xv = xa.codes.cpu().numpy().astype(np.float64) * np.repeat(xa.d.cpu().numpy()[:, :w_cols // 32], 32, axis=1)
+    for e in range(n):
+        W = np.stack([O.dequant_row(t, mats[e][i], w_cols) for i in range(w_rows)]).astype(np.float64)
+        for r in range(bounds[e], bounds[e + 1]):
+            want = W @ xv[r]
+            err = np.abs(got[ids[r], :w_rows] - want).max() / np.sqrt(np.mean(want ** 2))
+            assert err <= 1e-4, (e, r, err)
+    assert np.all(np.isnan(got[:, w_rows:]))   # nothing written past the rows' w_rows values

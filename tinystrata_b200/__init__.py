@@ -87,6 +87,7 @@ SIGNATURES = {
     "tsb_moe_decode_set_trace": (C.c_int, [_p]),
     "tsb_moe_decode_set_debug": (C.c_int, [C.c_int]),
     "tsb_add_scaled": (C.c_int, [_p, C.c_int, C.c_int, _p]),
+    "tsb_mmq_product": (C.c_int, [_p, C.c_int, _i64, _i64, C.c_uint64, C.c_int, _p, _p, _p, _i64, _p, _i64, _p]),
     "tsb_ep_unique_id": (C.c_int, [_p]),
     "tsb_ep_create": (C.c_int, [_p, C.c_int, C.c_int, C.POINTER(ExpertLayout), _p, C.c_uint64, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.c_int, _f, C.POINTER(C.c_void_p)]),
@@ -350,6 +351,20 @@ def moe_prefill_down(L: ExpertLayout, blobs, blob_stride: int, bounds, n_groups:
     _check(lib().tsb_moe_prefill_down(C.byref(L), _ptr(blobs), blob_stride, _ptr(bounds), n_groups, n_rows,
                                       C.c_void_p(h_act.data_ptr()), _ptr(out), _stream(stream)), "moe_prefill_down")
     return out
+
+
+def mmq_product(w, ggml_type: int, w_rows: int, w_cols: int, stride: int, n: int, x_act: MmqAct, bounds=None,
+                ids=None, total_rows: int | None = None, dst=None, ld_dst: int | None = None, stream=None):
+    """The grouped tensor-core product with fp32 output (tsb_mmq_product; mmq::Context::run / gemma4::Mmq::mul)."""
+    import torch
+    total_rows = x_act.rows if total_rows is None else total_rows
+    if dst is None:
+        dst = torch.empty((total_rows, w_rows), dtype=torch.float32, device=x_act.buf.device)
+    ld_dst = dst.stride(0) if ld_dst is None else ld_dst
+    _check(lib().tsb_mmq_product(_ptr(w), ggml_type, w_rows, w_cols, stride, n, C.c_void_p(x_act.data_ptr()),
+                                 _ptr(bounds), _ptr(ids), total_rows, _ptr(dst), ld_dst, _stream(stream)),
+           "mmq_product")
+    return dst
 
 
 def debug_mmq_block_sums(L: ExpertLayout, mode: int, blob, n_rows: int, x_act: MmqAct, stream=None):

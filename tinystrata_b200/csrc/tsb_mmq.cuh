@@ -92,7 +92,9 @@ struct MqParams {
     float* hd;
     float* hs;
     int ldh;
-    float* D;                  // down output: fp32 [n_rows][N]
+    float* D;                  // down output: fp32 rows of ld_d floats, row drow[r] (r when drow is null)
+    const int32_t* drow;
+    long long ld_d;
     int act;
     float limit;
     unsigned* err;
@@ -747,7 +749,8 @@ __global__ void __launch_bounds__(kMqThreads, 1)
             } else {
                 const int col = n0 + 64 * half;
                 if (row < row1 && col < p.N) {
-                    float4* dst = (float4*) (p.D + (size_t) row * p.N + col);
+                    const long long orow = p.drow ? (long long) __ldg(p.drow + row) : (long long) row;
+                    float4* dst = (float4*) (p.D + (size_t) orow * p.ld_d + col);
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
                         dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);

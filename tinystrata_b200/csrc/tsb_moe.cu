@@ -1111,6 +1111,8 @@ static int mq_run(const tsb_expert_layout* L, int mode, const void* blobs, uint6
         return mq_launch<MQ_GU>(L->gu_type, pp, xa, s, di);
     }
     pp.D = out;
+    pp.drow = nullptr;
+    pp.ld_d = pp.N;
     return mq_launch<MQ_DOWN>(L->d_type, pp, xa, s, di);
 }
 
@@ -1126,6 +1128,42 @@ int tsb_moe_prefill_down(const tsb_expert_layout* L, const void* blobs, uint64_t
                          int n_groups, int n_rows, const void* h_act, float* out, void* stream) {
     return mq_run(L, MQ_DOWN, blobs, blob_stride, bounds, n_groups, n_rows, h_act, nullptr, out, ACT_SWIGLU, INFINITY,
                   nullptr, cs(stream));
+}
+
+int tsb_mmq_product(const void* w, int ggml_type, int64_t w_rows, int64_t w_cols, uint64_t stride, int n,
+                    const void* x_act, const int32_t* bounds, const int32_t* ids, int64_t total_rows, float* dst,
+                    int64_t ld_dst, void* stream) {
+    if (total_rows == 0 || n == 0) return TSB_OK;
+    if (total_rows < 0 || total_rows > INT32_MAX || n < 0 || w_rows < 1 || w_rows > INT32_MAX || w_cols < 1 ||
+        w_cols > INT32_MAX || !dst || ld_dst < w_rows || (n > 1 && !bounds))
+        return fail(TSB_ERR_ARG, "mmq_product: arguments");
+    if (ld_dst % 4) return fail(TSB_ERR_ALIGN, "mmq_product: ld_dst a multiple of 4 floats");
+    // one expert blob per matrix: its rows are the "down" rows of a layout with n_ff = w_cols, n_embd = w_rows
+    tsb_expert_layout L{};
+    L.gu_type = ggml_type;
+    L.d_type = ggml_type;
+    L.n_embd = w_rows;
+    L.n_ff = w_cols;
+    L.gu_row = 0;
+    L.d_row = (uint64_t) tsb_row_bytes(ggml_type, w_cols);
+    L.up_off = 0;
+    L.down_off = 0;
+    L.bytes = L.d_row * (uint64_t) w_rows;
+    if (L.d_row == 0) return fail(TSB_ERR_UNSUPPORTED, "mmq_product: weight type %d", ggml_type);
+    int rc = mq_check(&L, w, stride, n, (int) total_rows, MQ_DOWN);
+    if (rc != TSB_OK) return rc;
+    if (!x_act) return fail(TSB_ERR_ARG, "mmq_product: null activations");
+    if ((uintptr_t) x_act % 256 || (uintptr_t) dst % 16) return fail(TSB_ERR_ALIGN, "mmq_product: buffer alignment");
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    MqParams pp = mq_params(&L, MQ_DOWN, w, stride, bounds, n, (int) total_rows);
+    pp.err = di->err;
+    pp.dbg = nullptr;
+    pp.D = dst;
+    pp.drow = ids;
+    pp.ld_d = ld_dst;
+    const MmqView xa = mmq_view(x_act, total_rows, pp.K);
+    return mq_launch<MQ_DOWN>(ggml_type, pp, xa, cs(stream), di);
 }
 
 int tsb_debug_mmq_block_sums(const tsb_expert_layout* L, int mode, const void* blob, int n_rows, const void* x_act,
