@@ -293,6 +293,35 @@ int tsb_ep_stats(const tsb_ep* ep, int64_t* sent, int64_t* received, int64_t* pi
 /* Free the buffers and the communicator (collective). */
 int tsb_ep_destroy(tsb_ep* ep);
 
+/* --------------------------------------------------------------------------------------------- GGUF files */
+/* A GGUF (v2 / v3) model file, memory-mapped read-only: metadata, tensor directory, and the repack of a layer's
+ * expert tensors into the native expert blobs above.  Replaces the parts of include/strata/artifact/gguf_reader.hpp the
+ * expert path needs and the blob build of src/qwen35/q36_engine.cu:1144-1167, 1196-1200.  Host memory only. */
+typedef struct tsb_gguf tsb_gguf;
+typedef struct tsb_gguf_tensor_info {
+    int32_t type, n_dims;
+    int64_t ne[4];         /* ne[0] innermost (values per row), as the file stores them */
+    uint64_t bytes;
+    const void* data;      /* inside the mapping; valid until tsb_gguf_close */
+} tsb_gguf_tensor_info;
+int tsb_gguf_open(const char* path, tsb_gguf** out);
+int tsb_gguf_close(tsb_gguf* g);
+int tsb_gguf_tensor_count(const tsb_gguf* g);
+int tsb_gguf_tensor_name(const tsb_gguf* g, int i, char* buf, int buf_bytes);
+int tsb_gguf_tensor(const tsb_gguf* g, const char* name, tsb_gguf_tensor_info* out);
+int tsb_gguf_kv_int(const tsb_gguf* g, const char* key, int64_t* value);
+int tsb_gguf_kv_float(const tsb_gguf* g, const char* key, double* value);
+int tsb_gguf_kv_str(const tsb_gguf* g, const char* key, char* buf, int buf_bytes);
+/* The layer whose tensors start with `prefix` (e.g. "blk.3."): its ffn_{gate,up,down}_exps types and shapes as a
+ * native expert layout, the blob stride (the blob rounded up to whole blocks of both types and 16 bytes, as the
+ * reference's engine places them) and the expert count. */
+int tsb_gguf_expert_layer(const tsb_gguf* g, const char* prefix, tsb_expert_layout* L, uint64_t* stride,
+                          int32_t* n_expert);
+/* Experts [first, first + count) of that layer as native expert blobs at dst + q * stride (host memory, zero bytes
+ * between a blob's end and the next), dst_bytes >= count * stride. */
+int tsb_gguf_repack_experts(const tsb_gguf* g, const char* prefix, int first, int count, void* dst,
+                            uint64_t dst_bytes);
+
 /* --------------------------------------------------------------------------------------------- test hook */
 /* The per-call integer sums and float values of one weight row (n values) against one q8_1 activation, as the
  * expert kernels compute them (calls in row_dot order, src/kernels/cuda/iq_kernels.cu:695-705).  Parity tests only. */

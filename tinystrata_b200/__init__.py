@@ -23,6 +23,12 @@ class TsbError(RuntimeError):
     pass
 
 
+class GgufTensorInfo(C.Structure):
+    """tsb_gguf_tensor_info: a tensor of a mapped GGUF file."""
+    _fields_ = [("type", C.c_int32), ("n_dims", C.c_int32), ("ne", C.c_int64 * 4), ("bytes", C.c_uint64),
+                ("data", C.c_void_p)]
+
+
 class DecodeLayer(C.Structure):
     """tsb_decode_layer: device pointers of one layer for the fused decode path."""
     _fields_ = [("blobs", C.c_void_p), ("router", C.c_void_p), ("sh_blob", C.c_void_p), ("logit_prior", C.c_void_p)]
@@ -88,6 +94,17 @@ SIGNATURES = {
     "tsb_moe_decode_set_debug": (C.c_int, [C.c_int]),
     "tsb_add_scaled": (C.c_int, [_p, C.c_int, C.c_int, _p]),
     "tsb_mmq_product": (C.c_int, [_p, C.c_int, _i64, _i64, C.c_uint64, C.c_int, _p, _p, _p, _i64, _p, _i64, _p]),
+    "tsb_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "tsb_gguf_close": (C.c_int, [_p]),
+    "tsb_gguf_tensor_count": (C.c_int, [_p]),
+    "tsb_gguf_tensor_name": (C.c_int, [_p, C.c_int, C.c_char_p, C.c_int]),
+    "tsb_gguf_tensor": (C.c_int, [_p, C.c_char_p, C.POINTER(GgufTensorInfo)]),
+    "tsb_gguf_kv_int": (C.c_int, [_p, C.c_char_p, C.POINTER(_i64)]),
+    "tsb_gguf_kv_float": (C.c_int, [_p, C.c_char_p, C.POINTER(C.c_double)]),
+    "tsb_gguf_kv_str": (C.c_int, [_p, C.c_char_p, C.c_char_p, C.c_int]),
+    "tsb_gguf_expert_layer": (C.c_int, [_p, C.c_char_p, C.POINTER(ExpertLayout), C.POINTER(C.c_uint64),
+                                        C.POINTER(C.c_int32)]),
+    "tsb_gguf_repack_experts": (C.c_int, [_p, C.c_char_p, C.c_int, C.c_int, _p, C.c_uint64]),
     "tsb_ep_unique_id": (C.c_int, [_p]),
     "tsb_ep_create": (C.c_int, [_p, C.c_int, C.c_int, C.POINTER(ExpertLayout), _p, C.c_uint64, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.c_int, _f, C.POINTER(C.c_void_p)]),

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsb_moe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["tsb_moe.cu", "tsb_decode.cu", "tsb_ep.cu"]
+SOURCES = ["tsb_moe.cu", "tsb_decode.cu", "tsb_ep.cu", "tsb_gguf.cpp"]
 # every header of the sources: a change to any of them rebuilds both objects
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cuh", ".inc"))) + ["../../include/tsb_moe.h"]
 FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",
@@ -40,7 +40,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(os.path.join(HERE, "_build"), exist_ok=True)
     procs = []
     for s in srcs:
-        obj = os.path.join(HERE, "_build", s.replace(".cu", ".o"))
+        obj = os.path.join(HERE, "_build", os.path.splitext(s)[0] + ".o")
         objs.append(obj)
         if force or _stale(obj, deps):
             cmd = [NVCC, *FLAGS, "-c", os.path.join(CSRC, s), "-o", obj]

@@ -12,13 +12,12 @@
 //     Q8_0 codes, Q4_K nibbles, Q6_K codes - 32, IQ3 signed grid bytes) in the same swizzled layout, and stage the
 //     per-(row, block) scale terms;
 //   * one thread issues one tcgen05.mma.kind::i8 M128 N128 K32 per 32-value block (Q6_K: two, one per 16-value half,
-//     the other half's weight codes zero) into one of four int32 block-sum buffers in tensor memory.  The buffers are
-//     pre-loaded with the integer 0x4B400000 and accumulated into, so a buffer ends holding the float bits of
-//     1.5 * 2^23 + S for the block sum S (|S| < 2^22): the conversion to fp32 costs no instruction, and
-//     fma(fb, d_x, -d_x * 1.5 * 2^23) is d_x * S rounded once (d_x * 1.5 * 2^23 is exact);
-//   * eight epilogue warps (two per tensor-memory lane quarter, 64 columns each) read a block's sums, re-arm the
-//     buffer with the bias (tcgen05.st), and add d_w (d_x S) into fp32 register accumulators block after block -- the
-//     reference's per-block scaling, two FMAs per output per block;
+//     the other half's weight codes zero) into one of four int32 block-sum buffers in tensor memory;
+//   * eight epilogue warps (two per tensor-memory lane quarter, 64 columns each) read a block's sums, add the word
+//     0x4B400000 to each (an integer add: the float bits of 1.5 * 2^23 + S for the block sum S, |S| < 2^22, so no
+//     conversion instruction; fma(fb, d_x, -d_x * 1.5 * 2^23) is d_x * S rounded once, d_x * 1.5 * 2^23 being exact)
+//     and add d_w (d_x S) into fp32 register accumulators block after block with packed FMAs -- the reference's
+//     per-block scaling, two FMAs per output per block;
 //   * gate/up tiles interleave the matrices in 32-row groups (B rows 0-31 gate, 32-63 up of the same hidden values,
 //     64-95 gate, 96-127 up of the next 32), so a thread's 64 columns are the gate and up sums of one q8_1 block of
 //     hidden values: the activation, the q8_1 quantisation (the reference's arithmetic) and the store of the hidden
@@ -124,15 +123,6 @@ __device__ __forceinline__ void tmem_ld32u(uint32_t addr, uint32_t (&r)[32]) {
                    "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
                    "=r"(r[30]), "=r"(r[31])
                  : "r"(addr));
-}
-// 32 columns of this warp's lane quarter set to the same word (the bias the next block's MMA accumulates onto), in
-// stores of 8 columns: a store's source registers are distinct registers in the machine code, and 32 copies of the word
-// next to a block's 64 sums and 64 accumulators would spill.
-__device__ __forceinline__ void tmem_fill32(uint32_t addr, uint32_t v) {
-#pragma unroll
-    for (int c = 0; c < 32; c += 8)
-        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(addr + c), "r"(v)
-                     : "memory");
 }
 // Two columns at once: a += w * (fma(f, dx, ndxm)) with the packed fp32 pipe instructions (the same IEEE roundings as
 // two scalar fma pairs, half the instructions).  The intrinsic, not inline assembly: the compiler schedules it.
@@ -406,17 +396,6 @@ __global__ void __launch_bounds__(kMqThreads, 1)
     const int q = warp & 3;                              // an epilogue warp's tensor-memory lane quarter (warp % 4)
     const int half = (warp - kMqEpi0) >> 2;              // ... and its 64 columns (warps 3-6: 0..63, 7-10: 64..127)
     const uint32_t lane_base = tmem + ((uint32_t) (q * 32) << 16) + (uint32_t) (64 * half);
-    if (warp >= kMqEpi0) {   // arm every buffer with the bias before the first MMA
-#pragma unroll
-        for (int b = 0; b < kMqBufs; ++b) {
-            tmem_fill32(lane_base + b * 128, kMqMagic);
-            tmem_fill32(lane_base + b * 128 + 32, kMqMagic);
-        }
-        tmem_wait_st();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
 
     const int n_mt = gtile[G];
     const int per_tile = MODE == MQ_GU ? 64 : kMqBN;   // hidden values (gate/up) or output columns per tile
@@ -567,7 +546,7 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                                 break;
                             }
                             tc_fence_after();
-                            mq_mma(tmem + (uint32_t) buf * 128, pf_sdesc(a0 + 32 * b), pf_sdesc(b0 + h * kMqTile + 32 * b), 1u);
+                            mq_mma(tmem + (uint32_t) buf * 128, pf_sdesc(a0 + 32 * b), pf_sdesc(b0 + h * kMqTile + 32 * b), 0u);
                             pf_commit(&t_full[buf]);
                         }
                     }
@@ -620,7 +599,7 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                         if (dbg_tile && tile == (int) blockIdx.x) {
                             int32_t* d = p.dbg + ((size_t) (ks * kMqBlk + b) * 128 + rl) * 128 + 64 * half;
 #pragma unroll
-                            for (int j = 0; j < 64; ++j) d[j] = (int32_t) (fb(j) - kMqMagic);
+                            for (int j = 0; j < 64; ++j) d[j] = (int32_t) fb(j);
                         }
                         if constexpr (WT == T_IQ3_XXS) {
                             // the reference's integer step (ls S + S / 2) / 2 (C division), then d_x times it
@@ -633,7 +612,7 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                                 uint32_t vb[4];
 #pragma unroll
                                 for (int k = 0; k < 4; ++k) {
-                                    const int S = (int) (fb(4 * j4 + k) - kMqMagic);
+                                    const int S = (int) fb(4 * j4 + k);
                                     vb[k] = (uint32_t) ((ls[k] * S + S / 2) / 2) + kMqMagic;
                                 }
                                 mq_fma2(acc[4 * j4], acc[4 * j4 + 1], w.x, w.y, vb[0], vb[1], dx, ndxm);
@@ -643,8 +622,10 @@ __global__ void __launch_bounds__(kMqThreads, 1)
 #pragma unroll
                             for (int j4 = 0; j4 < 16; ++j4) {
                                 const float4 w = lds4(w4 + j4);
-                                mq_fma2(acc[4 * j4], acc[4 * j4 + 1], w.x, w.y, fb(4 * j4), fb(4 * j4 + 1), dx, ndxm);
-                                mq_fma2(acc[4 * j4 + 2], acc[4 * j4 + 3], w.z, w.w, fb(4 * j4 + 2), fb(4 * j4 + 3), dx, ndxm);
+                                mq_fma2(acc[4 * j4], acc[4 * j4 + 1], w.x, w.y, fb(4 * j4) + kMqMagic,
+                                        fb(4 * j4 + 1) + kMqMagic, dx, ndxm);
+                                mq_fma2(acc[4 * j4 + 2], acc[4 * j4 + 3], w.z, w.w, fb(4 * j4 + 2) + kMqMagic,
+                                        fb(4 * j4 + 3) + kMqMagic, dx, ndxm);
                             }
                             if constexpr (F::kSx) {   // Q4_K's min term: - (dmin m) (d_x sum q_x)
                                 const float sx = b == 0 ? sx4.x : b == 1 ? sx4.y : b == 2 ? sx4.z : sx4.w;
@@ -657,10 +638,6 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                                 }
                             }
                         }
-                        // re-arm the buffer once its sums are consumed (the registers that held them are free)
-                        tmem_fill32(lane_base + buf0 * 128, kMqMagic);
-                        tmem_fill32(lane_base + buf0 * 128 + 32, kMqMagic);
-                        tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&t_empty[buf0]);
@@ -673,27 +650,28 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                             tmem_ld32u(lane_base + buf0 * 128 + 32 * c, fa);
                             tmem_ld32u(lane_base + buf1 * 128 + 32 * c, fc);
                             tmem_wait_ld();
-                            tmem_fill32(lane_base + buf0 * 128 + 32 * c, kMqMagic);
-                            tmem_fill32(lane_base + buf1 * 128 + 32 * c, kMqMagic);
                             if (dbg_tile && tile == (int) blockIdx.x) {
                                 int32_t* d = p.dbg + ((size_t) (ks * kMqBlk + b) * 2 * 128 + rl) * 128 + 64 * half + 32 * c;
 #pragma unroll
                                 for (int j = 0; j < 32; ++j) {
-                                    d[j] = (int32_t) (fa[j] - kMqMagic);
-                                    d[128 * 128 + j] = (int32_t) (fc[j] - kMqMagic);
+                                    d[j] = (int32_t) fa[j];
+                                    d[128 * 128 + j] = (int32_t) fc[j];
                                 }
                             }
 #pragma unroll
                             for (int j4 = 0; j4 < 8; ++j4) {
                                 const float4 wa = lds4(w4 + 8 * c + j4), wb = lds4(v4 + 8 * c + j4);
                                 float* a = acc + 32 * c + 4 * j4;
-                                mq_fma2(a[0], a[1], wa.x, wa.y, fa[4 * j4], fa[4 * j4 + 1], dx, ndxm);
-                                mq_fma2(a[2], a[3], wa.z, wa.w, fa[4 * j4 + 2], fa[4 * j4 + 3], dx, ndxm);
-                                mq_fma2(a[0], a[1], wb.x, wb.y, fc[4 * j4], fc[4 * j4 + 1], dx, ndxm);
-                                mq_fma2(a[2], a[3], wb.z, wb.w, fc[4 * j4 + 2], fc[4 * j4 + 3], dx, ndxm);
+                                mq_fma2(a[0], a[1], wa.x, wa.y, fa[4 * j4] + kMqMagic, fa[4 * j4 + 1] + kMqMagic, dx,
+                                        ndxm);
+                                mq_fma2(a[2], a[3], wa.z, wa.w, fa[4 * j4 + 2] + kMqMagic, fa[4 * j4 + 3] + kMqMagic,
+                                        dx, ndxm);
+                                mq_fma2(a[0], a[1], wb.x, wb.y, fc[4 * j4] + kMqMagic, fc[4 * j4 + 1] + kMqMagic, dx,
+                                        ndxm);
+                                mq_fma2(a[2], a[3], wb.z, wb.w, fc[4 * j4 + 2] + kMqMagic, fc[4 * j4 + 3] + kMqMagic,
+                                        dx, ndxm);
                             }
                         }
-                        tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) {
