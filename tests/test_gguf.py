@@ -100,10 +100,10 @@ def test_gguf_layer_runs_through_the_expert_path(tmp_path, cuda):
     import tinystrata_b200 as T
     from tinystrata_b200.gguf import GGUFFile
     from tinystrata_b200.layer import MoELayer, PrefillLayer
-    cfg = dict(synth.QWEN, n_expert=16)
+    cfg = dict(synth.QWEN, n_expert=32)
     layer = synth.make_layer(cfg, 11)
     path = tmp_path / "q.gguf"
-    _write_model(path, cfg, [layer], 16)
+    _write_model(path, cfg, [layer], 32)
     sh = torch.from_numpy(layer["sh_blob"]).to(cuda)
     x = torch.from_numpy(synth.rms_normed(np.random.default_rng(11), 64, cfg["n_embd"])).to(cuda)
     with GGUFFile(str(path)) as g:
