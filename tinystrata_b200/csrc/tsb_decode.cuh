@@ -562,15 +562,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         S.abort = 1;
     };
 
-    // P1 units: the same CTA range every layer; this warp's are r1.lo + warp + j kDecWarps
-    const Range r1 = split(p1_units(p), gridDim.x, blockIdx.x);
-    const int n1w = per_warp(r1.hi - r1.lo, warp);
+    // P1 units: the same ones every layer, dealt to the CTAs round robin (unit u to CTA u % grid: the router half rows
+    // and the T-times heavier shared gate/up pairs mix on every CTA); this warp's j-th is p1_unit(j)
+    const int n1 = p1_units(p);
+    const int n1c = (int) blockIdx.x < n1 ? (n1 - (int) blockIdx.x + (int) gridDim.x - 1) / (int) gridDim.x : 0;
+    const int n1w = per_warp(n1c, warp);
+    auto p1_unit = [&](int j) { return (int) blockIdx.x + (int) gridDim.x * (warp + j * kDecWarps); };
     int pre1 = 0;   // P1 units of the coming layer already issued
     {
         const DecLayer L0 = p.layers[0];
         while (pre1 < n1w && st.can_issue()) {
             BulkCopy c[2];
-            const int n = p1_copies(p, L0, r1.lo + warp + pre1 * kDecWarps, c);
+            const int n = p1_copies(p, L0, p1_unit(pre1), c);
             st.issue(c, n, lane);
             ++pre1;
         }
@@ -630,7 +633,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                     fail(0x331u, l);
                     break;
                 }
-                const int u = r1.lo + warp + j * kDecWarps;
+                const int u = p1_unit(j);
                 if (u < 2 * (E + 1)) {
                     const int o = u >> 1, half = u & 1;
                     const float4* wr = (const float4*) buf;
@@ -689,7 +692,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 st.release();
                 if (next1 < n1w) {
                     BulkCopy c[2];
-                    const int n = p1_copies(p, L, r1.lo + warp + next1 * kDecWarps, c);
+                    const int n = p1_copies(p, L, p1_unit(next1), c);
                     st.issue(c, n, lane);
                     ++next1;
                 }
@@ -822,9 +825,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
         const int ng = S.n_groups;
 
         // This warp's units after the routing, in stream order: its P2 units, its P3 units, the next layer's P1 units.
+        // P2 units are dealt to the CTAs round robin (unit u to CTA u % grid): the shared down units, which sit after
+        // the routed ones and cost T times a routed unit, spread over every CTA instead of landing on the last few
         const int n2 = p2_units(p, ng), nrt = p2_rt_units(p, ng);
-        const Range r2 = split(n2, gridDim.x, blockIdx.x);
-        const int n2w = per_warp(r2.hi - r2.lo, warp);
+        const int n2c = (int) blockIdx.x < n2 ? (n2 - (int) blockIdx.x + (int) gridDim.x - 1) / (int) gridDim.x : 0;
+        const int n2w = per_warp(n2c, warp);
+        auto p2_unit = [&](int j) { return (int) blockIdx.x + (int) gridDim.x * (warp + j * kDecWarps); };
         const Range ch = my_chunks(p);
         const int nch = ch.hi - ch.lo, ntask = nch * ng;
         const int n3w = per_warp(p3_units(p, ng), warp);
@@ -836,11 +842,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
             BulkCopy c[2];
             int n;
             if (post < n2w)
-                n = p2_copies(p, L, S, ng, r2.lo + warp + post * kDecWarps, c);
+                n = p2_copies(p, L, S, ng, p2_unit(post), c);
             else if (post < n2w + n3w)
                 n = p3_copies(p, L, S, ng, ch, warp + (post - n2w) * kDecWarps, c);
             else
-                n = p1_copies(p, Ln, r1.lo + warp + (post - n2w - n3w) * kDecWarps, c);
+                n = p1_copies(p, Ln, p1_unit(post - n2w - n3w), c);
             st.issue(c, n, lane);
             ++post;
         };
@@ -857,7 +863,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) k_decode_layers(DecParams p) {
                 fail(0x332u, l);
                 break;
             }
-            const int u = r2.lo + warp + j * kDecWarps;
+            const int u = p2_unit(j);
             if (u < nrt) {
                 const int i0 = u * p.rt_per_unit, i1 = min(i0 + p.rt_per_unit, ng * F);
                 for (int i = i0; i < i1; ++i) {   // the unit's gate rows, then its up rows
