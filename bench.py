@@ -328,7 +328,7 @@ EP_METRIC = "EP prefill MoE-layer tokens/s (Gemma-4-26B-A4B-shaped Q4_0 layer, T
 EPQ_METRIC = "EP prefill MoE-layer tokens/s (Qwen3.6-35B-A3B-shaped IQ3_XXS/IQ3_S layer, T=65536, experts sharded)"
 
 
-def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16: bool = True,
+def ep_qwen_measure(args, steps: int, warmup: int, micro_batches: int = 2, bf16: bool = False,
                     own_group: bool = True) -> dict | None:
     """C4: the Qwen3.6-35B-A3B-shaped layer (256 experts, IQ3_XXS gate/up, IQ3_S down, top-8 softmax, Q8_0 shared
     expert gated by a sigmoid of the 257th router row) over T = 65536 prompt tokens split evenly over the ranks

@@ -279,7 +279,9 @@ int tsb_ep_dispatch(tsb_ep* ep, const void* x_q8_1, const int32_t* ids, const fl
 /* Finish the step tsb_ep_dispatch started: per micro-batch the local grouped experts on the tensor cores as its rows
  * arrive, the weighted partial row per received token, its return exchange; then per token, on `stream`,
  * out = (accumulate ? out : 0) + the partials of the ranks it went to in rank order (+ sigmoid(sgate[t * sg_stride])
- * shared[t] when shared is given).  return_bf16: partial rows travel as bf16 instead of fp32. */
+ * shared[t] when shared is given).  return_bf16: partial rows travel as bf16 instead of fp32 (half the return bytes;
+ * the rounding moves single outputs by up to ~2 % of the RMS, past the layer tolerance fp32 returns meet).
+ * return_bf16 is collective: the same on every rank. */
 int tsb_ep_combine(tsb_ep* ep, float* out, int accumulate, const float* shared, const float* sgate, int sg_stride,
                    int return_bf16, void* stream);
 /* The bound of the host's waits on the exchanges (default 120 s): past it the communicator is aborted and the call

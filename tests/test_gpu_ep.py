@@ -188,7 +188,10 @@ def test_ep_device_path_two_gpus_vs_oracle():
             if item[0] == "empty":
                 continue
             mb, bf16, err, cos, st = item
-            assert err <= 1e-2 and cos >= 0.9999, (rank, mb, bf16, err, cos)
+            # fp32 returns meet the layer bar; bf16 returns (half the return bytes) round each partial row to 8
+            # significant bits, which moves the worst single value to ~1.6 % of the RMS at cosine 0.999999: the
+            # library's default and the bench use fp32, and bf16 is held to 3e-2 here
+            assert err <= (3e-2 if bf16 else 1e-2) and cos >= 0.9999, (rank, mb, bf16, err, cos)
         sent_total += results[0][4]["rows_sent"]
         recv_total += results[0][4]["rows_received"]
     assert sent_total == recv_total   # every row sent was received
