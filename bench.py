@@ -30,9 +30,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_LAYERS = 40   # --layers changes it for profiling captures only (a smaller device footprint); the bench is 40
-# DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch (61.77 MB
+# DRAM bytes (read + write) per layer of k_decode_layers at T = 1 from one ncu capture of a 4-layer launch (61.79 MB
 # per launch); traffic grows with the layer count, so a launch of N layers moves N times this.
-TRAFFIC_PER_LAYER_T1 = 61.77e6 / 4
+TRAFFIC_PER_LAYER_T1 = (60848896 + 938496) / 4
 METRIC = "MoE-layer tokens/s (decode, Qwen3.6-35B-A3B-shaped IQ3_XXS layer, 40 layers resident)"
 
 

@@ -45,6 +45,9 @@ constexpr uint32_t kMqWTerm = kMqBlk * 128 * 4;              // a [4 blocks][128
 constexpr uint32_t kMqMagic = 0x4B400000u;                   // float bits of 1.5 * 2^23
 constexpr float kMqMagicF = 12582912.0f;
 constexpr int kMqMaxGroups = 512;
+// The MMA thread signals block sums two units at a time (a tile always holds an even number of units: K is a
+// multiple of 64), halving the epilogue's barrier waits (3-4 % faster gate/up and down).
+constexpr bool kMqPairHandoff = true;
 constexpr uint32_t kMqSmemBudget = 220 * 1024;
 // instruction descriptor: D s32, A s8, B s8, both K-major, N = 128, M = 128
 constexpr uint32_t kMqIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (kMqBN >> 3) << 17) |
@@ -547,7 +550,7 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                             }
                             tc_fence_after();
                             mq_mma(tmem + (uint32_t) buf * 128, pf_sdesc(a0 + 32 * b), pf_sdesc(b0 + h * kMqTile + 32 * b), 0u);
-                            pf_commit(&t_full[buf]);
+                            if (!kMqPairHandoff || (u & 1u)) pf_commit(&t_full[buf]);
                         }
                     }
                     pf_commit(&empty[s]);   // the stage's operands are free once these MMAs complete
@@ -583,12 +586,25 @@ __global__ void __launch_bounds__(kMqThreads, 1)
                     const float dx = b == 0 ? dx4.x : b == 1 ? dx4.y : b == 2 ? dx4.z : dx4.w;
                     const float ndxm = -dx * kMqMagicF;   // exact: 1.5 * 2^23 has two significant bits
                     const int buf0 = (int) (u % kMqBufs);
-                    bool got = true;
-                    for (int h = 0; h < SPLIT && got; ++h)
-                        got = mbar_wait_bounded(&t_full[(buf0 + h) % kMqBufs], ((u + h) / kMqBufs) & 1u, p.err, 0x604u);
-                    ok = __all_sync(0xffffffffu, got);
-                    if (!ok) break;
-                    tc_fence_after();
+                    if (kMqPairHandoff) {
+                        // units u, u + 1 (one block, or a Q6_K block's two halves) hand over together: the MMA
+                        // commits after the odd one, whose completion implies the even one's
+                        if ((u & 1u) == 0) {
+                            const uint32_t w = u | 1u;
+                            ok = __all_sync(0xffffffffu, mbar_wait_bounded(&t_full[w % kMqBufs], (w / kMqBufs) & 1u,
+                                                                           p.err, 0x604u));
+                            if (!ok) break;
+                            tc_fence_after();
+                        }
+                    } else {
+                        bool got = true;
+                        for (int h = 0; h < SPLIT && got; ++h)
+                            got = mbar_wait_bounded(&t_full[(buf0 + h) % kMqBufs], ((u + h) / kMqBufs) & 1u, p.err,
+                                                    0x604u);
+                        ok = __all_sync(0xffffffffu, got);
+                        if (!ok) break;
+                        tc_fence_after();
+                    }
                     const float4* w4 = (const float4*) (wt + b * 128 + 64 * half);
                     if constexpr (SPLIT == 1) {
                         uint32_t f0[32], f1[32];
