@@ -112,6 +112,8 @@ def _ep_worker(rank, world, port, q, scenario):
         for i, (mb, bf16, T_tok) in enumerate(steps):
             if scenario == "timeout" and i == 1 and rank == 1:
                 q.put((rank, "left", None))
+                q.close()
+                q.join_thread()   # the message is out of this process before it ends
                 os._exit(0)   # between steps, nothing in flight: the peer never answers the next exchange
             rng = np.random.default_rng(80 + 10 * rank + i)
             x = synth.rms_normed(rng, T_tok, H) if T_tok else np.zeros((0, H), np.float32)
