@@ -181,8 +181,8 @@ def verify_decode(cfg, D, layers, x0_dev, priors, stream):
 
 PREFILL_METRIC = "MoE-layer tokens/s (prefill, Gemma-4-26B-A4B-shaped Q4_0 layer, T=8192)"
 PREFILL_LFM_METRIC = "MoE-layer tokens/s (prefill, LFM2.5-24B-A2B-shaped Q4_K/Q6_K layer, T=2048)"
-# int8 operations per layer of the C2 configuration: 2 T (K 3 H F + 3 H FS) + router 2 T H E (algorithmic, the
-# reference's MMQ work; the kernels here issue two fp16 tensor-core products per block, hi and lo weight parts)
+# int8 operations per layer of the C2 configuration: 2 T (K 3 H F + 3 H FS) + router 2 T H E (algorithmic: the
+# reference's MMQ work, one int8 multiply-add per weight value and routed row, whatever the kernels issue)
 def prefill_ops(T, H, F, FS, K, E):
     return 2.0 * T * (K * 3 * H * F + 3 * H * FS) + 2.0 * T * H * E
 
