@@ -252,6 +252,35 @@ int tsb_moe_decode_set_trace(unsigned long long* buf);
  * Process-wide.  No counterpart in the reference. */
 int tsb_moe_decode_set_debug(int withhold_cta);
 
+/* --------------------------------------------------------------------------------------------- small products */
+/* Up to TSB_MMVQ_MAX matrices of one ggml type and shape [n_out][n_in] in one launch, each times its own q8_1 column
+ * (n_in / 32 blocks): y[i][r] = row r of w[i] . x[i], each value the reference's iq_mmvq row dot bit for bit (the
+ * same calls, lanes and sum order).  Replaces gemma_native_mmvq_slots / gemma_native_mmvq_ids
+ * (include/strata/gemma4/matvec.hpp:143-171: the Gemma 4 / LFM2 cached-expert decode step).  Formats Q4_0, Q8_0,
+ * Q4_K, Q6_K, IQ3_XXS, IQ3_S (tsb_mmvq_supported); others return TSB_ERR_UNSUPPORTED and launch nothing, where the
+ * reference's call returns false. */
+#define TSB_MMVQ_MAX 32
+typedef struct tsb_mmvq_slots {
+    const void* w[TSB_MMVQ_MAX];
+    const void* x[TSB_MMVQ_MAX];
+    float* y[TSB_MMVQ_MAX];
+} tsb_mmvq_slots;
+/* The same with the matrices the device picked: matrix j = table[ids[j]] + offset bytes (table and ids on the device),
+ * column x + (j / x_every) * x_stride bytes, output y + j * y_stride floats. */
+typedef struct tsb_mmvq_ids {
+    const void* const* table;
+    const int32_t* ids;
+    uint64_t offset;
+    const void* x;
+    uint64_t x_stride;
+    int32_t x_every;
+    float* y;
+    uint64_t y_stride;
+} tsb_mmvq_ids;
+int tsb_mmvq_supported(int ggml_type);
+int tsb_mmvq_run_slots(int ggml_type, const tsb_mmvq_slots* slots, int count, int n_in, int n_out, void* stream);
+int tsb_mmvq_run_ids(int ggml_type, const tsb_mmvq_ids* m, int count, int n_in, int n_out, void* stream);
+
 /* --------------------------------------------------------------------------------------------- expert parallelism */
 /* Prompt-path experts sharded over the ranks of one node (one process per GPU), dispatch and return over NCCL
  * point-to-point exchanges on NVLink.  The reference runs one GPU per engine; the per-rank body is its prompt branch

@@ -3,6 +3,7 @@
 // the router's argument error as the reference raises it.  Needs no GPU.
 #include "strata/kernels/iq_kernels.hpp"
 #include "strata/kernels/native_router.hpp"
+#include "strata/gemma4/matvec.hpp"
 #include "strata/prefill/moe_mmq.hpp"
 #include "gemma4/mmq.hpp"
 
@@ -37,5 +38,11 @@ int main() {
         threw = true;
     }
     std::printf("{\"kind\": \"router_error\", \"threw\": %d}\n", (int) threw);
+    strata::kernels::MmvqSlots slots{};   // a format without a kernel here: false, nothing launched (no GPU needed)
+    std::printf("{\"kind\": \"mmvq\", \"ids_q4_0\": %d, \"ids_iq3_xxs\": %d, \"ids_q5_0\": %d, \"slots_q5_0\": %d}\n",
+                (int) strata::kernels::gemma_native_mmvq_ids_supported(2),
+                (int) strata::kernels::gemma_native_mmvq_ids_supported(18),
+                (int) strata::kernels::gemma_native_mmvq_ids_supported(6),
+                (int) strata::kernels::gemma_native_mmvq_slots(6, slots, 1, 2048, 64, nullptr));
     return 0;
 }

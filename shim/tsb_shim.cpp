@@ -2,13 +2,14 @@
 // TinyStrata's engines link against the B200 path with their call sites unchanged.  Compiled against the
 // reference's own headers (include/strata/..., src/gemma4/mmq.hpp), which pin every signature; a maintainer adds it to
 // the engine target in place of the reference's definitions (src/kernels/cuda/iq_kernels.cu, native_router.cu,
-// src/gemma4/kernels.cu, src/gemma4/mmq.cu, src/prefill/moe_mmq.cu for the functions below).
+// src/gemma4/kernels.cu, src/gemma4/matvec.cu, src/gemma4/mmq.cu, src/prefill/moe_mmq.cu for the functions below).
 //
 // Error behaviour is the reference's: iq_kernels.cu prints and exits on a bad launch, native_router.cu and the MMQ
 // wrappers throw std::runtime_error / std::invalid_argument; the C ABI's status is turned back into that.
 #include "strata/kernels/iq_kernels.hpp"
 #include "strata/kernels/native_router.hpp"
 #include "strata/gemma4/kernels.hpp"
+#include "strata/gemma4/matvec.hpp"
 #include "strata/prefill/moe_mmq.hpp"
 #include "gemma4/mmq.hpp"
 #include "tsb_moe.h"
@@ -103,6 +104,41 @@ void native_router_topk(const float* logits, int32_t* ids, float* weights, int n
                         void* stream) {
     if (tsb_native_router_topk(logits, ids, weights, n_expert, k, n_tok, n_expert, stream) != TSB_OK)
         throw std::invalid_argument(tsb_last_error());   // native_router.cu:103-110
+}
+
+// ------------------------------------------------------------------------------ include/strata/gemma4/matvec.hpp
+// The cached-expert decode products: false (nothing launched) for a format without a kernel here, as the reference.
+bool gemma_native_mmvq_slots(int ggml_type, const MmvqSlots& slots, int count, int n_in, int n_out, void* stream) {
+    if (tsb_mmvq_supported(ggml_type) != 1) return false;
+    tsb_mmvq_slots s{};
+    for (int i = 0; i < count && i < kMmvqSlotsMax; ++i) {
+        s.w[i] = slots.w[i];
+        s.x[i] = slots.x[i];
+        s.y[i] = slots.y[i];
+    }
+    const int rc = tsb_mmvq_run_slots(ggml_type, &s, count, n_in, n_out, stream);
+    if (rc == TSB_ERR_UNSUPPORTED) return false;
+    die(rc, "gemma_native_mmvq_slots");
+    return true;
+}
+
+bool gemma_native_mmvq_ids_supported(int ggml_type) { return tsb_mmvq_supported(ggml_type) == 1; }
+
+bool gemma_native_mmvq_ids(int ggml_type, const MmvqIds& ids, int count, int n_in, int n_out, void* stream) {
+    if (tsb_mmvq_supported(ggml_type) != 1) return false;
+    tsb_mmvq_ids m{};
+    m.table = ids.table;
+    m.ids = ids.ids;
+    m.offset = ids.offset;
+    m.x = ids.x;
+    m.x_stride = ids.x_stride;
+    m.x_every = ids.x_every;
+    m.y = ids.y;
+    m.y_stride = ids.y_stride;
+    const int rc = tsb_mmvq_run_ids(ggml_type, &m, count, n_in, n_out, stream);
+    if (rc == TSB_ERR_UNSUPPORTED) return false;
+    die(rc, "gemma_native_mmvq_ids");
+    return true;
 }
 
 }  // namespace strata::kernels

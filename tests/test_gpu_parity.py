@@ -381,3 +381,54 @@ def test_moe_layer_qwen_end_to_end(cuda):
     err, cos = layer_tolerance(x.cpu().numpy(), ref["out"])
     assert err <= 1e-2 and cos >= 0.9999, (err, cos)
     assert T.device_error() == 0
+
+
+# ------------------------------------------------------------------------------------------------ slot products
+@pytest.mark.parametrize("t,n_in,n_out", [(synth.T_Q4_0, 2816, 704), (synth.T_Q4_0, 704, 2816), (synth.T_Q8_0, 2048, 512),
+                                          (synth.T_Q4_K, 2048, 1792), (synth.T_Q6_K, 1792, 2048),
+                                          (synth.T_IQ3_XXS, 2048, 512), (synth.T_IQ3_S, 512, 2048)])
+def test_mmvq_slots_and_ids_vs_reference_mmvq(cuda, t, n_in, n_out):
+    """tsb_mmvq_run_slots / _ids (gemma_native_mmvq_slots / _ids): 32 matrices, each with its own q8_1 column, in one
+    launch, against the reference's own iq_mmvq one matrix at a time on the same buffers -- bit for bit for the
+    formats whose call values carry no fused multiply-add, within 1e-6 relative otherwise -- and the ids form (device
+    table of matrices, ids with repeats, columns shared by x_every entries) against the slots form."""
+    R = ref_or_skip()
+    rng = np.random.default_rng(200 + t)
+    n = 32
+    rb = synth.row_bytes(t, n_in)
+    mats = [dev(synth.gen_matrix(rng, t, n_out, n_in, 0.02)) for _ in range(n)]
+    xs = [dev(O.quantize_q8_1(rng.normal(0, 1, size=(1, n_in)).astype(np.float32))[0]) for _ in range(n)]
+    ys = [torch.full((n_out,), float("nan"), device="cuda") for _ in range(n)]
+    T.mmvq_slots(t, mats, xs, ys, n_in, n_out)
+    ref = [torch.zeros(n_out, device="cuda") for _ in range(n)]
+    if t != synth.T_Q6_K:   # the reference's iq_mmvq has no Q6_K (STRATA_MMVQ_FMTS, iq_kernels.cu:705): the oracle
+        for i in range(n):
+            R.ref_iq_mmvq(t, refgpu.ptr(mats[i]), refgpu.ptr(xs[i]), refgpu.ptr(ref[i]), n_in, n_out, 1,
+                          refgpu.stream())
+    torch.cuda.synchronize()
+    assert T.device_error() == 0
+    for i in range(n):
+        a = ys[i].cpu().numpy()
+        if t == synth.T_Q6_K:
+            b = O.mat_vec(t, mats[i].cpu().numpy(), xs[i].cpu().numpy(), n_in, n_out)
+            assert np.allclose(a, b, rtol=1e-5, atol=1e-5 * np.abs(b).max()), i
+            continue
+        b = ref[i].cpu().numpy()
+        if t in EXACT_FLOAT:
+            assert np.array_equal(a, b), i
+        else:
+            assert np.allclose(a, b, rtol=1e-6, atol=1e-6 * np.abs(b).max()), i
+    # the ids form: matrix j = table[ids[j]], column j // 4, outputs y_stride apart
+    table = torch.tensor([m.data_ptr() for m in mats], dtype=torch.int64, device="cuda")
+    ids = torch.from_numpy(rng.integers(0, n, size=16).astype(np.int32)).cuda()
+    xcat = torch.stack(xs[:4])                       # 4 columns, each shared by 4 entries
+    y_stride = n_out + 16
+    ycat = torch.full((16, y_stride), float("nan"), device="cuda")
+    T.mmvq_ids(t, table, ids, 0, xcat, xcat.stride(0), 4, ycat, y_stride, 16, n_in, n_out)
+    want = [torch.full((n_out,), float("nan"), device="cuda") for _ in range(16)]
+    idl = ids.cpu().tolist()
+    T.mmvq_slots(t, [mats[idl[j]] for j in range(16)], [xs[j // 4] for j in range(16)], want, n_in, n_out)
+    torch.cuda.synchronize()
+    for j in range(16):
+        assert torch.equal(ycat[j, :n_out], want[j]), j
+    assert torch.isnan(ycat[:, n_out:]).all()

@@ -63,3 +63,9 @@ def test_shim_formats_and_mmq_queries(shim_lines):
 
 def test_shim_turns_a_refused_call_into_the_reference_exception(shim_lines):
     assert [r for r in shim_lines if r["kind"] == "router_error"][0]["threw"] == 1
+
+
+def test_shim_slot_products_report_their_formats(shim_lines):
+    m = [r for r in shim_lines if r["kind"] == "mmvq"][0]
+    assert m["ids_q4_0"] == 1 and m["ids_iq3_xxs"] == 1
+    assert m["ids_q5_0"] == 0 and m["slots_q5_0"] == 0   # the reference's "no kernel for it": false, nothing launched

@@ -29,6 +29,17 @@ class GgufTensorInfo(C.Structure):
                 ("data", C.c_void_p)]
 
 
+class MmvqSlots(C.Structure):
+    """tsb_mmvq_slots (the reference's MmvqSlots, include/strata/gemma4/matvec.hpp:149-153)."""
+    _fields_ = [("w", C.c_void_p * 32), ("x", C.c_void_p * 32), ("y", C.c_void_p * 32)]
+
+
+class MmvqIds(C.Structure):
+    """tsb_mmvq_ids (the reference's MmvqIds, include/strata/gemma4/matvec.hpp:158-167)."""
+    _fields_ = [("table", C.c_void_p), ("ids", C.c_void_p), ("offset", C.c_uint64), ("x", C.c_void_p),
+                ("x_stride", C.c_uint64), ("x_every", C.c_int32), ("y", C.c_void_p), ("y_stride", C.c_uint64)]
+
+
 class DecodeLayer(C.Structure):
     """tsb_decode_layer: device pointers of one layer for the fused decode path."""
     _fields_ = [("blobs", C.c_void_p), ("router", C.c_void_p), ("sh_blob", C.c_void_p), ("logit_prior", C.c_void_p)]
@@ -105,6 +116,9 @@ SIGNATURES = {
     "tsb_gguf_expert_layer": (C.c_int, [_p, C.c_char_p, C.POINTER(ExpertLayout), C.POINTER(C.c_uint64),
                                         C.POINTER(C.c_int32)]),
     "tsb_gguf_repack_experts": (C.c_int, [_p, C.c_char_p, C.c_int, C.c_int, _p, C.c_uint64]),
+    "tsb_mmvq_supported": (C.c_int, [C.c_int]),
+    "tsb_mmvq_run_slots": (C.c_int, [C.c_int, C.POINTER(MmvqSlots), C.c_int, C.c_int, C.c_int, _p]),
+    "tsb_mmvq_run_ids": (C.c_int, [C.c_int, C.POINTER(MmvqIds), C.c_int, C.c_int, C.c_int, _p]),
     "tsb_ep_unique_id": (C.c_int, [_p]),
     "tsb_ep_create": (C.c_int, [_p, C.c_int, C.c_int, C.POINTER(ExpertLayout), _p, C.c_uint64, C.c_int, C.c_int,
                                 C.c_int, C.c_int, C.c_int, _f, C.POINTER(C.c_void_p)]),
@@ -382,6 +396,21 @@ def mmq_product(w, ggml_type: int, w_rows: int, w_cols: int, stride: int, n: int
                                  _ptr(bounds), _ptr(ids), total_rows, _ptr(dst), ld_dst, _stream(stream)),
            "mmq_product")
     return dst
+
+
+def mmvq_slots(ggml_type: int, ws, xs, ys, n_in: int, n_out: int, stream=None):
+    """Up to 32 products y[i] = W[i] x[i] (q8_1 columns) in one launch (gemma_native_mmvq_slots)."""
+    S = MmvqSlots()
+    for i, (w, x, y) in enumerate(zip(ws, xs, ys)):
+        S.w[i], S.x[i], S.y[i] = w.data_ptr(), x.data_ptr(), y.data_ptr()
+    _check(lib().tsb_mmvq_run_slots(ggml_type, C.byref(S), len(ws), n_in, n_out, _stream(stream)), "mmvq_run_slots")
+
+
+def mmvq_ids(ggml_type: int, table, ids, offset: int, x, x_stride: int, x_every: int, y, y_stride: int, count: int,
+             n_in: int, n_out: int, stream=None):
+    """The products of matrices table[ids[j]] + offset (device table and ids), gemma_native_mmvq_ids."""
+    M = MmvqIds(table.data_ptr(), ids.data_ptr(), offset, x.data_ptr(), x_stride, x_every, y.data_ptr(), y_stride)
+    _check(lib().tsb_mmvq_run_ids(ggml_type, C.byref(M), count, n_in, n_out, _stream(stream)), "mmvq_run_ids")
 
 
 def debug_mmq_block_sums(L: ExpertLayout, mode: int, blob, n_rows: int, x_act: MmqAct, stream=None):

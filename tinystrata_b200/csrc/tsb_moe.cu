@@ -4,6 +4,7 @@
 #include "tsb_prefill.cuh"
 #include "tsb_prefill_k.cuh"
 #include "tsb_mmq.cuh"
+#include "tsb_mmvq.cuh"
 #include "tsb_act_layout.cuh"
 #include "../../include/tsb_moe.h"
 
@@ -1164,6 +1165,91 @@ int tsb_mmq_product(const void* w, int ggml_type, int64_t w_rows, int64_t w_cols
     pp.ld_d = ld_dst;
     const MmqView xa = mmq_view(x_act, total_rows, pp.K);
     return mq_launch<MQ_DOWN>(ggml_type, pp, xa, cs(stream), di);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------ many small matrix-vector products
+template <int TY, int J>
+static int mv_launch_t(const MvArgs& a, int count, cudaStream_t s, DevInfo* di) {
+    constexpr int TB = table_bytes<TY>();
+    auto kern = k_mmvq<TY, J>;
+    if (TB > 48 * 1024) {   // the IQ3 tables: a per-device opt-in, bits 48..55
+        const int bit = 48 + (TY == T_IQ3_S ? 4 : 0) + (J == 1 ? 0 : J == 2 ? 1 : J == 4 ? 2 : 3);
+        const int rc = smem_optin(di, bit, kern, TB, "mmvq: shared memory");
+        if (rc != TSB_OK) return rc;
+    }
+    const long long want = (2LL * di->sms + count - 1) / count;
+    const long long gx = std::max<long long>(1, std::min<long long>((a.n_out + 7) / 8, want));
+    kern<<<dim3((unsigned) gx, (unsigned) count), 256, TB, s>>>(a);
+    return cuda_status("mmvq");
+}
+template <int TY>
+static int mv_launch(const MvArgs& a, int count, cudaStream_t s, DevInfo* di) {
+    const int C = a.n_in / qk_of(TY) * cpb_of(TY);
+    if (C <= 32) return mv_launch_t<TY, 1>(a, count, s, di);
+    if (C <= 64) return mv_launch_t<TY, 2>(a, count, s, di);
+    if (C <= 128) return mv_launch_t<TY, 4>(a, count, s, di);
+    if (C <= 256) return mv_launch_t<TY, 8>(a, count, s, di);
+    return fail(TSB_ERR_UNSUPPORTED, "mmvq: %d calls per row (at most 256)", C);
+}
+static int mv_run(int t, MvArgs& a, int count, int n_in, int n_out, cudaStream_t s) {
+    if (count < 0 || count > kMvMax || n_in <= 0 || n_out < 0)
+        return fail(TSB_ERR_ARG, "mmvq: 0..%d matrices, positive n_in", kMvMax);
+    if (qk_of(t) == 0) return fail(TSB_ERR_UNSUPPORTED, "mmvq: weight type %d", t);
+    if (n_in % qk_of(t) || n_in % 32) return fail(TSB_ERR_UNSUPPORTED, "mmvq: rows of whole %d-value blocks", qk_of(t));
+    if (count == 0 || n_out == 0) return TSB_OK;
+    DevInfo* di = dev_info();
+    if (!di) return fail(TSB_ERR_CUDA, "no CUDA device");
+    a.n_in = n_in;
+    a.n_out = n_out;
+    a.row_bytes = (uint32_t) (n_in / qk_of(t) * bb_of(t));
+    switch (t) {
+        case T_Q4_0: return mv_launch<T_Q4_0>(a, count, s, di);
+        case T_Q8_0: return mv_launch<T_Q8_0>(a, count, s, di);
+        case T_Q4_K: return mv_launch<T_Q4_K>(a, count, s, di);
+        case T_Q6_K: return mv_launch<T_Q6_K>(a, count, s, di);
+        case T_IQ3_XXS: return mv_launch<T_IQ3_XXS>(a, count, s, di);
+        case T_IQ3_S: return mv_launch<T_IQ3_S>(a, count, s, di);
+        default: return fail(TSB_ERR_UNSUPPORTED, "mmvq: weight type %d", t);
+    }
+}
+
+extern "C" {
+
+int tsb_mmvq_supported(int ggml_type) { return qk_of(ggml_type) != 0 ? 1 : 0; }
+
+int tsb_mmvq_run_slots(int ggml_type, const tsb_mmvq_slots* slots, int count, int n_in, int n_out, void* stream) {
+    if (!slots) return fail(TSB_ERR_ARG, "mmvq_run_slots: null slots");
+    MvArgs a{};
+    for (int i = 0; i < count && i < kMvMax; ++i) {
+        if (!slots->w[i] || !slots->x[i] || !slots->y[i]) return fail(TSB_ERR_ARG, "mmvq_slots: null pointer in slot %d", i);
+        if ((uintptr_t) slots->w[i] % 2 || (uintptr_t) slots->x[i] % 4 || (uintptr_t) slots->y[i] % 4)
+            return fail(TSB_ERR_ALIGN, "mmvq_slots: slot %d alignment", i);
+        a.w[i] = slots->w[i];
+        a.x[i] = slots->x[i];
+        a.y[i] = slots->y[i];
+    }
+    a.by_ids = 0;
+    return mv_run(ggml_type, a, count, n_in, n_out, cs(stream));
+}
+
+int tsb_mmvq_run_ids(int ggml_type, const tsb_mmvq_ids* m, int count, int n_in, int n_out, void* stream) {
+    if (!m || !m->table || !m->ids || !m->x || !m->y || m->x_every < 1)
+        return fail(TSB_ERR_ARG, "mmvq_ids: arguments");
+    if (m->offset % 2 || (uintptr_t) m->x % 4 || m->x_stride % 4 || (uintptr_t) m->y % 4)
+        return fail(TSB_ERR_ALIGN, "mmvq_ids: alignment");
+    MvArgs a{};
+    a.by_ids = 1;
+    a.table = m->table;
+    a.ids = m->ids;
+    a.offset = m->offset;
+    a.xb = (const uint8_t*) m->x;
+    a.x_stride = m->x_stride;
+    a.x_every = m->x_every;
+    a.yb = m->y;
+    a.y_stride = m->y_stride;
+    return mv_run(ggml_type, a, count, n_in, n_out, cs(stream));
 }
 
 int tsb_debug_mmq_block_sums(const tsb_expert_layout* L, int mode, const void* blob, int n_rows, const void* x_act,
