@@ -281,6 +281,42 @@ int tsb_mmvq_supported(int ggml_type);
 int tsb_mmvq_run_slots(int ggml_type, const tsb_mmvq_slots* slots, int count, int n_in, int n_out, void* stream);
 int tsb_mmvq_run_ids(int ggml_type, const tsb_mmvq_ids* m, int count, int n_in, int n_out, void* stream);
 
+/* ------------------------------------------------------------------------------------------- host-staged experts */
+/* A layer whose experts do not all sit in HBM: n_slots of them in device slots (expert x in slot slot_of[x] >= 0, at
+ * slots + slot_of[x] * stride), every expert's blob in host memory at host_blobs + x * stride (n_expert * stride bytes,
+ * pinned and mapped for the device: cudaHostAlloc, or cudaHostRegister with cudaHostRegisterMapped).  Replaces the
+ * reference's hybrid mode (src/qwen35/q36_engine.cu: k_group_hy 423-452, moe_hybrid_gpu / moe_hybrid_cpu /
+ * k_merge_cpu 3052-3210, rebalance 3215-3265, the streamed layer 2995-3049).  Where the reference runs the entries
+ * of experts without a slot on a CPU thread pool, here the GPU pulls those experts' blobs over the host link itself
+ * and runs every entry through the grouped expert kernels: outputs equal a resident layer's bit for bit. */
+
+/* Grouping as tsb_moe_group (slot_of, device array [n_expert]; ids outside [0, n_expert) are dropped), each group's
+ * blob at its expert's slot or, for an expert without one, at the next free blob of stage (stage_cap blobs of stride
+ * bytes, stage_cap >= min(n_ent, n_expert)), which the same call fills from host_blobs on `stream` (device loads of
+ * the mapped host memory: no host synchronisation, graph-capturable).  counts (optional, device [n_expert]) += the
+ * entries of each expert: the usage a placement reads between steps.  stride a multiple of 16. */
+int tsb_moe_group_staged(const int32_t* ids, int n_ent, int K, int n_expert, const int32_t* slot_of, int n_slots,
+                         const void* slots, const void* host_blobs, uint64_t stride, void* stage, int stage_cap,
+                         uint64_t* grp_ptr, int32_t* grp_start, int32_t* n_groups, int32_t* ent_dst, int32_t* ent_tok,
+                         uint32_t* counts, void* stream);
+/* Host arrays.  The reference's rebalance for one layer: experts by score (highest first, ties the lower id), slots
+ * by their resident's score (lowest first, ties the lower slot); each top-n_slots expert without a slot takes the
+ * next such slot while its resident scores lower, up to max_swaps moves; then every score is halved (the age).
+ * Writes the moves (expert, slot) and updates slot_of / exp_in_slot; returns the number of moves (>= 0).  With no
+ * partial residency (n_slots 0 or n_expert) nothing changes, scores included. */
+int tsb_staged_rebalance(double* score, int n_expert, int n_slots, int32_t* slot_of, int32_t* exp_in_slot,
+                         int max_swaps, int32_t* move_expert, int32_t* move_slot);
+/* The moves' blobs (blob_bytes each) host to device into their slots on `stream`; upload slot_of after them on the
+ * same stream so that no step reads a slot before its blob. */
+int tsb_staged_load(const void* host_blobs, void* slots, uint64_t stride, uint64_t blob_bytes, const int32_t* move_expert,
+                    const int32_t* move_slot, int n_moves, int n_expert, int n_slots, void* stream);
+/* The streamed layer of the prompt path: every expert's blob into stage in expert order (n_expert * stride bytes),
+ * runs of consecutive slots holding consecutive experts device to device and runs of experts without a slot host to
+ * device; the whole layer in one host copy when fewer than half the experts are resident or `whole` is set.
+ * slot_of is a HOST array here.  Returns the number of copies issued (> 0) or a negative status. */
+int tsb_stage_layer(const int32_t* slot_of, int n_expert, int n_slots, const void* slots, const void* host_blobs,
+                    uint64_t stride, void* stage, int whole, void* stream);
+
 /* --------------------------------------------------------------------------------------------- expert parallelism */
 /* Prompt-path experts sharded over the ranks of one node (one process per GPU), dispatch and return over NCCL
  * point-to-point exchanges on NVLink.  The reference runs one GPU per engine; the per-rank body is its prompt branch

@@ -249,6 +249,39 @@ def dispatch(ids: np.ndarray, n_expert: int):
     return bounds, dst, src, inv, mx
 
 
+def staged_rebalance(score: np.ndarray, slot_of: np.ndarray, exp_in_slot: np.ndarray, max_swaps: int):
+    """The hybrid mode's placement of one layer, src/qwen35/q36_engine.cu:3215-3265 (the non-fair scan), with
+    std::sort's unspecified tie order fixed as the lower id / lower slot first, and the age of
+    include/strata/qwen35/cache_policy.hpp:28-30.  Updates the arrays in place; returns the moves [(expert, slot)]."""
+    E, S = score.size, exp_in_slot.size
+    moves = []
+    if S <= 0 or S >= E:
+        return moves
+    order = sorted(range(E), key=lambda x: (-score[x], x))
+    victims = sorted(range(S), key=lambda s: (score[exp_in_slot[s]], s))
+    vi, left = 0, max_swaps
+    for i in range(S):
+        if left <= 0:
+            break
+        x = order[i]
+        if slot_of[x] >= 0:
+            continue
+        if vi >= len(victims):
+            break
+        s = victims[vi]
+        y = exp_in_slot[s]
+        if score[y] >= score[x]:
+            break
+        vi += 1
+        slot_of[y] = -1
+        slot_of[x] = s
+        exp_in_slot[s] = x
+        moves.append((x, s))
+        left -= 1
+    score *= 0.5
+    return moves
+
+
 # ------------------------------------------------------------------------------------------------ experts
 def expert_ffn(gu_type: int, d_type: int, blob: np.ndarray, n_embd: int, n_ff: int, xq_row: np.ndarray,
                act: int = ACT_SWIGLU, limit: float = float("inf"), want_h: bool = False):

@@ -130,6 +130,11 @@ SIGNATURES = {
     "tsb_ep_destroy": (C.c_int, [_p]),
     "tsb_moe_layer_tail": (C.c_int, [_p, _p, _p, _p, _p, _f, C.c_int, C.c_int, _f, _p]),
     "tsb_set_wait_limit_ns": (C.c_int, [_u64]),
+    "tsb_moe_group_staged": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, _p, C.c_int, _p, _p, _u64, _p, C.c_int, _p, _p,
+                                       _p, _p, _p, _p, _p]),
+    "tsb_staged_rebalance": (C.c_int, [_p, C.c_int, C.c_int, _p, _p, C.c_int, _p, _p]),
+    "tsb_staged_load": (C.c_int, [_p, _p, _u64, _u64, _p, _p, C.c_int, C.c_int, C.c_int, _p]),
+    "tsb_stage_layer": (C.c_int, [_p, C.c_int, C.c_int, _p, _p, _u64, _p, C.c_int, _p]),
 }
 
 
@@ -260,6 +265,53 @@ def moe_group(ids, n_expert: int, blobs, blob_stride: int, groups: Groups | None
                                _ptr(groups.grp_start), _ptr(groups.n_groups), _ptr(groups.ent_dst),
                                _ptr(groups.ent_tok), _stream(stream)), "moe_group")
     return groups
+
+
+def moe_group_staged(ids, n_expert: int, slot_of, n_slots: int, slots, host_blobs, blob_stride: int, stage,
+                     stage_cap: int, groups: Groups | None = None, counts=None, stream=None) -> Groups:
+    """Grouping of a host-staged layer (k_group_hy, q36_engine.cu:423-452, with the missed experts fetched into
+    stage by the GPU): slot_of int32 [n_expert] on the device, host_blobs a pinned host tensor."""
+    T, K = ids.shape
+    groups = groups or Groups(T * K, ids.device)
+    _check(lib().tsb_moe_group_staged(_ptr(ids), T * K, K, n_expert, _ptr(slot_of), n_slots, _ptr(slots),
+                                      _ptr(host_blobs), blob_stride, _ptr(stage), stage_cap, _ptr(groups.grp_ptr),
+                                      _ptr(groups.grp_start), _ptr(groups.n_groups), _ptr(groups.ent_dst),
+                                      _ptr(groups.ent_tok), _ptr(counts), _stream(stream)), "moe_group_staged")
+    return groups
+
+
+def staged_rebalance(score, slot_of, exp_in_slot, max_swaps: int):
+    """The reference's rebalance of one layer (q36_engine.cu:3215-3265) on host numpy arrays (score float64,
+    slot_of / exp_in_slot int32, updated in place).  Returns the moves as (experts, slots) int32 arrays."""
+    import numpy as np
+    for a, dt in ((score, np.float64), (slot_of, np.int32), (exp_in_slot, np.int32)):
+        assert a.dtype == dt and a.flags.c_contiguous
+    me = np.zeros(max(max_swaps, 1), np.int32)
+    ms = np.zeros(max(max_swaps, 1), np.int32)
+    n = lib().tsb_staged_rebalance(score.ctypes.data, score.size, exp_in_slot.size, slot_of.ctypes.data,
+                                   exp_in_slot.ctypes.data, max_swaps, me.ctypes.data, ms.ctypes.data)
+    _check(min(n, 0), "staged_rebalance")
+    return me[:n], ms[:n]
+
+
+def staged_load(host_blobs, slots, blob_stride: int, blob_bytes: int, move_expert, move_slot, n_expert: int,
+                n_slots: int, stream=None):
+    """The moved experts' blobs host to device into their slots (cudaMemcpyAsync on `stream`)."""
+    _check(lib().tsb_staged_load(_ptr(host_blobs), _ptr(slots), blob_stride, blob_bytes, move_expert.ctypes.data,
+                                 move_slot.ctypes.data, len(move_expert), n_expert, n_slots, _stream(stream)),
+           "staged_load")
+
+
+def stage_layer(slot_of, n_slots: int, slots, host_blobs, blob_stride: int, stage, whole: bool = False,
+                stream=None) -> int:
+    """The streamed prompt layer (stream_kick, q36_engine.cu:3001-3033): every blob into stage in expert order;
+    slot_of a host int32 numpy array.  Returns the copies issued."""
+    import numpy as np
+    assert slot_of.dtype == np.int32 and slot_of.flags.c_contiguous
+    n = lib().tsb_stage_layer(slot_of.ctypes.data, slot_of.size, n_slots, _ptr(slots), _ptr(host_blobs), blob_stride,
+                              _ptr(stage), int(whole), _stream(stream))
+    _check(min(n, 0), "stage_layer")
+    return n
 
 
 def native_expert_grouped(L: ExpertLayout, groups: Groups, cap_groups: int, cap_entries: int, x_q8_1, scratch, out,
@@ -566,4 +618,4 @@ class DecodeStack:
         return int(code[0])
 
 
-from .layer import MoELayer  # noqa: E402  (host mirror of the engines' MoE block)
+from .layer import MoELayer, StagedExperts  # noqa: E402  (host mirror of the engines' MoE block)

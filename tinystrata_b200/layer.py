@@ -9,8 +9,60 @@ from __future__ import annotations
 
 import torch
 
-from . import (ACT_SWIGLU, Groups, Q8_1_BYTES, moe_combine, moe_group, moe_sum, native_expert_grouped,
-               native_expert_layout, native_expert_scratch_bytes, native_router_topk, route_rows, router_logits_f32)
+import numpy as np
+
+from . import (ACT_SWIGLU, Groups, Q8_1_BYTES, moe_combine, moe_group, moe_group_staged, moe_sum,
+               native_expert_grouped, native_expert_layout, native_expert_scratch_bytes, native_router_topk,
+               route_rows, router_logits_f32, staged_load, staged_rebalance)
+
+
+class StagedExperts:
+    """A layer's experts in pinned host memory, n_slots of them resident in HBM slots: the reference's hybrid-mode
+    state of a layer (q36_engine.cu: slot_of / exp_in_slot / score, k_group_hy 423-452, rebalance 3215-3265).
+
+    host_blobs: pinned uint8 [E, stride] (every expert); resident: the experts to place first (default 0..n_slots-1).
+    Entries of experts without a slot are fetched by the GPU into a stage buffer of min(max_entries, E) blobs."""
+
+    def __init__(self, host_blobs: torch.Tensor, blob_bytes: int, n_slots: int, max_entries: int, device,
+                 resident=None, stream=None):
+        assert host_blobs.is_pinned() and host_blobs.dim() == 2 and host_blobs.dtype == torch.uint8
+        self.host = host_blobs
+        self.E, self.stride = host_blobs.shape[0], int(host_blobs.stride(0))
+        self.blob_bytes, self.n_slots = int(blob_bytes), int(n_slots)
+        assert 0 <= self.n_slots <= self.E
+        self.slots = torch.empty((max(self.n_slots, 1), self.stride), dtype=torch.uint8, device=device)
+        self.stage_cap = min(max_entries, self.E)
+        self.stage = torch.empty((self.stage_cap, self.stride), dtype=torch.uint8, device=device)
+        self.counts = torch.zeros(self.E, dtype=torch.int32, device=device)
+        self.score = np.zeros(self.E, np.float64)
+        self.slot_of = np.full(self.E, -1, np.int32)
+        first = np.arange(self.n_slots, dtype=np.int32) if resident is None else np.asarray(resident, np.int32)
+        assert first.size == self.n_slots and len(set(first.tolist())) == first.size
+        self.exp_in_slot = first.copy()
+        self.slot_of[first] = np.arange(self.n_slots, dtype=np.int32)
+        self.slot_of_d = torch.from_numpy(self.slot_of).to(device)
+        staged_load(self.host, self.slots, self.stride, self.blob_bytes, first, np.arange(self.n_slots, dtype=np.int32),
+                    self.E, self.n_slots, stream=stream)
+        self.swaps = 0
+
+    def group(self, ids, groups: Groups, stream=None) -> Groups:
+        return moe_group_staged(ids, self.E, self.slot_of_d, self.n_slots, self.slots, self.host, self.stride,
+                                self.stage, self.stage_cap, groups, counts=self.counts, stream=stream)
+
+    def rebalance(self, max_swaps: int, stream=None) -> int:
+        """Between steps: the usage counts into the scores, the reference's placement, the moved blobs and the new
+        slot table uploaded on `stream` (in that order).  Reads the counts (a host synchronisation)."""
+        cs = torch.cuda.current_stream() if stream is None else stream
+        with torch.cuda.stream(cs):
+            self.score += self.counts.cpu().numpy().astype(np.float64)
+            self.counts.zero_()
+            me, ms = staged_rebalance(self.score, self.slot_of, self.exp_in_slot, max_swaps)
+            if len(me):
+                staged_load(self.host, self.slots, self.stride, self.blob_bytes, me, ms, self.E, self.n_slots,
+                            stream=cs)
+                self.slot_of_d.copy_(torch.from_numpy(self.slot_of))
+        self.swaps += len(me)
+        return len(me)
 
 
 class MoELayer:
@@ -19,15 +71,20 @@ class MoELayer:
     blobs: uint8 [E, blob_bytes] (the layer's expert blobs); router: fp32 [E (+1), H]; sh_blob: uint8 [bytes] or None.
     """
 
-    def __init__(self, cfg: dict, blobs: torch.Tensor, router: torch.Tensor, sh_blob: torch.Tensor | None = None,
-                 max_tokens: int = 16, escale=None, bias=None):
+    def __init__(self, cfg: dict, blobs: torch.Tensor | None, router: torch.Tensor, sh_blob: torch.Tensor | None = None,
+                 max_tokens: int = 16, escale=None, bias=None, staged: StagedExperts | None = None):
         self.cfg = cfg
         self.H, self.F, self.E, self.K = cfg["n_embd"], cfg["n_ff"], cfg["n_expert"], cfg["n_used"]
-        self.dev = blobs.device
+        self.dev = router.device
         self.blobs, self.router, self.sh_blob = blobs, router.contiguous(), sh_blob
+        self.staged = staged
         self.L = native_expert_layout(cfg["gu_type"], cfg["d_type"], self.H, self.F)
-        assert blobs.shape[-1] == self.L.bytes
-        self.stride = int(blobs.stride(0)) if blobs.dim() > 1 else int(self.L.bytes)
+        if staged is not None:
+            assert blobs is None and staged.E == self.E and staged.blob_bytes == self.L.bytes
+            self.stride = staged.stride
+        else:
+            assert blobs.shape[-1] == self.L.bytes
+            self.stride = int(blobs.stride(0)) if blobs.dim() > 1 else int(self.L.bytes)
         self.escale, self.bias = escale, bias
         self.max_tokens = max_tokens
         n_ent = max_tokens * self.K
@@ -83,7 +140,10 @@ class MoELayer:
                                 stream=stream)
             self.ids[:T].copy_(ids)
             self.w[:T].copy_(w)
-        moe_group(self.ids[:T], E, self.blobs, self.stride, self.groups, stream=stream)
+        if self.staged is not None:
+            self.staged.group(self.ids[:T], self.groups, stream=stream)
+        else:
+            moe_group(self.ids[:T], E, self.blobs, self.stride, self.groups, stream=stream)
         n_ent = T * K
         native_expert_grouped(self.L, self.groups, n_ent, n_ent, hq, self.scratch, self.parts, cfg["act"],
                               cfg.get("limit", float("inf")), stream=stream)
