@@ -554,6 +554,96 @@ def bench_ep(args):
     return 0
 
 
+def bench_staged(args):
+    """Host-staged experts: one Qwen-shaped decode layer (256 IQ3_XXS experts) whose experts all sit in pinned host
+    memory, 64 of them in HBM slots; T tokens a step.  The layer-by-layer step (router, top-8, staged grouping with the
+    missed experts pulled over the host link by the GPU, experts, shared expert, combine) as a CUDA graph, timed
+    beside the same step on the resident layer, and the grouping + fetch alone (CUDA events on its stream) for the
+    host-link rate.  Per step a new token: its picks miss the slots about 3 times in 4."""
+    import torch
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+    from tinystrata_b200.layer import MoELayer, StagedExperts
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = synth.QWEN
+    T, H, K, E = args.tokens, cfg["n_embd"], cfg["n_used"], cfg["n_expert"]
+    n_slots = 64
+    st = synth.device_layers(cfg, 1, seed=5, device=device)
+    blobs, router, sh = st["blobs"][0], st["routers"][0], st["sh_blobs"][0]
+    nb = blobs.shape[1]
+    stride = (nb + 15) // 16 * 16
+    host = torch.zeros((E, stride), dtype=torch.uint8).pin_memory()
+    host[:, :nb].copy_(blobs.cpu())
+    S = StagedExperts(host, nb, n_slots, T * K, device)
+    R = MoELayer(cfg, blobs, router, sh, max_tokens=T)
+    M = MoELayer(cfg, None, router, sh, max_tokens=T, staged=S)
+    n_in = args.steps + args.warmup
+    rng = np.random.default_rng(5)
+    xs_all = torch.from_numpy(np.stack([synth.rms_normed(rng, T, H) for _ in range(n_in)])).to(device)
+    hd = torch.empty((T, H), device=device)
+    hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
+    x = torch.zeros((T, H), device=device)
+    s = torch.cuda.Stream()
+    graphs = {}
+    for name, layer in (("staged", M), ("resident", R)):
+        with torch.cuda.stream(s):
+            hd.copy_(xs_all[0])
+            TS.quantize_q8_1_rows(hd, hq, stream=s)
+            layer.forward(x, hd, hq, stream=s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            TS.quantize_q8_1_rows(hd, hq, stream=s)
+            layer.forward(x, hd, hq, stream=s)
+        graphs[name] = g
+    res = {}
+    with Clocks(0) as clk:
+        for name in ("staged", "resident"):
+            g = graphs[name]
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_in)]
+            with torch.cuda.stream(s):
+                for i in range(n_in):
+                    hd.copy_(xs_all[i])
+                    evs[i][0].record(s)
+                    g.replay()
+                    evs[i][1].record(s)
+            torch.cuda.synchronize()
+            res[name] = float(np.mean([a.elapsed_time(b) for a, b in evs[args.warmup:]])) * 1e3
+        # the grouping + fetch alone, on the routing of each step's token
+        fetch_us, fetched = [], 0
+        for i in range(n_in):
+            with torch.cuda.stream(s):
+                hd.copy_(xs_all[i])
+                TS.quantize_q8_1_rows(hd, hq, stream=s)
+                M.forward(x, hd, hq, stream=s)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(s)
+                S.group(M.ids[:T], M.groups, stream=s)
+                b.record(s)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                fetch_us.append(a.elapsed_time(b) * 1e3)
+                fetched += sum(1 for e in np.unique(M.ids[:T].cpu().numpy()) if S.slot_of[e] < 0)
+    assert TS.device_error() == 0
+    f_us = float(np.mean(fetch_us))
+    per_step = fetched / args.steps
+    line = {
+        "metric": "staged decode layer time", "value": res["staged"], "unit": "us per layer", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "dtype": "q8_1 x IQ3_XXS",
+        "data": "synthetic",
+        "config": {"workload": f"decode T={T}, one Qwen3.6-shaped layer, 256 IQ3_XXS experts in pinned host memory, "
+                               f"{n_slots} in HBM slots", "slots": n_slots, "tokens": T},
+        "resident_us_per_layer": res["resident"],
+        "fetch": {"us_per_step": f_us, "experts_per_step": per_step, "blob_bytes": int(nb),
+                  "host_link_GBps": per_step * nb / (f_us * 1e-6) / 1e9},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -567,11 +657,15 @@ def main():
                     help="decode only: without the C2 / C3 prefill and C4 expert-parallel keys")
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen", "staged"],
                     help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192); "
                          "prefill_lfm: the C3 LFM2-shaped layer (--tokens 2048); ep: the C2 layer expert-parallel "
-                         "over the launched ranks; ep_qwen: the C4 Qwen IQ3 layer expert-parallel (65536 tokens)")
+                         "over the launched ranks; ep_qwen: the C4 Qwen IQ3 layer expert-parallel (65536 tokens); "
+                         "staged: a decode layer with its experts in host memory, 64 of 256 in HBM slots")
     args = ap.parse_args()
+    if args.workload == "staged":
+        return bench_staged(args)
     if args.workload == "ep_qwen":
         return bench_ep_qwen(args)
     if args.workload in ("prefill", "prefill_lfm", "ep"):
