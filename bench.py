@@ -9,7 +9,7 @@ each rank runs its own replica (weak scaling) and `value` sums the replicas.
 
 The same line carries the other configurations as keys: decode_sweep (T = 2, 4, 16), prefill_c2 (Gemma-4-shaped Q4_0
 layer, T = 8192) and prefill_c3 (LFM2.5-shaped Q4_K / Q6_K layer, T = 2048) on one GPU, each with its CPU baseline
-where one exists, and ep_c4 (the Qwen IQ3 layer over T = 65536 tokens, experts sharded over every rank of the run).
+where one exists, gemma_lfm_decode (the Gemma 4 / LFM2 decode layer, layer by layer and in one launch), and ep_c4 (the Qwen IQ3 layer over T = 65536 tokens, experts sharded over every rank of the run).
 --workload selects one of them alone.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl tsb|reference]
@@ -554,6 +554,79 @@ def bench_ep(args):
     return 0
 
 
+def act_decode_measure(device, steps: int = 30, warmup: int = 5) -> dict:
+    """The Gemma 4 and LFM2 decode MoE layer (one layer, every expert resident) at T = 1 and 4: the layer-by-layer
+    entry points (route_rows, grouping, grouped experts, moe_sum, the dense shared MLP) and the one-launch block
+    (tsb_moe_decode_act), each as a CUDA graph with the input's q8_1, a new token per step and L2 flushed (a 256 MB
+    write) between steps; CUDA events around each replay.  The two paths' outputs are compared bit for bit first."""
+    import torch
+    import tinystrata_b200 as TS
+    from tinystrata_b200 import synth
+
+    res = {}
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    s = torch.cuda.Stream(device)
+    for name, cfg in (("gemma", synth.GEMMA), ("lfm", synth.LFM)):
+        st = synth.device_layers(cfg, 1, seed=31, device=device)
+        H, E, K = cfg["n_embd"], cfg["n_expert"], cfg["n_used"]
+        kw = ({"escale": torch.ones(E, device=device)} if cfg["router_mode"] == "softmax_scaled"
+              else {"bias": torch.zeros(E, device=device)})
+        sh = st["sh_blobs"][0] if cfg.get("sh_n_ff") else None
+        blob_bytes = int(st["blobs"].shape[-1])
+        sh_bytes = int(sh.numel()) if sh is not None else 0
+        for T in (1, 4):
+            M = TS.MoELayer(cfg, st["blobs"][0], st["routers"][0], sh, max_tokens=T, **kw)
+            n_in = warmup + steps
+            rng = np.random.default_rng(T)
+            xs = torch.from_numpy(np.stack([synth.rms_normed(rng, T, H) for _ in range(n_in)])).to(device)
+            hd = torch.empty((T, H), device=device)
+            hq = torch.empty((T, H // 32 * 36), dtype=torch.uint8, device=device)
+            x = torch.zeros((T, H), device=device)
+            # bit-for-bit check of the two paths on the first input
+            hd.copy_(xs[0])
+            TS.quantize_q8_1_rows(hd, hq)
+            xa, xb = torch.zeros_like(x), torch.zeros_like(x)
+            M.forward(xa, hd, hq)
+            M.forward_fused(xb, hd, hq)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(xa, xb))
+            out = {"bitwise_equal": same}
+            for path in ("layerwise", "fused"):
+                fwd = M.forward if path == "layerwise" else M.forward_fused
+                with torch.cuda.stream(s):
+                    TS.quantize_q8_1_rows(hd, hq, stream=s)
+                    fwd(x, hd, hq, stream=s)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    TS.quantize_q8_1_rows(hd, hq, stream=s)
+                    fwd(x, hd, hq, stream=s)
+                times, bytes_ = [], []
+                for i in range(n_in):
+                    with torch.cuda.stream(s):
+                        hd.copy_(xs[i])
+                        flush.fill_(i & 255)
+                        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        a.record(s)
+                        g.replay()
+                        b.record(s)
+                    torch.cuda.synchronize()
+                    if i >= warmup:
+                        times.append(a.elapsed_time(b) * 1e3)
+                        n_dist = len(np.unique(M.ids[:T].cpu().numpy()))
+                        bytes_.append(E * H * 4 + n_dist * blob_bytes + sh_bytes)
+                del g
+                us = float(np.mean(times))
+                out[f"{path}_us_per_layer"] = us
+                if path == "fused":
+                    out["fused_hbm_gbs"] = float(np.mean(bytes_)) / (us * 1e-6) / 1e9
+                    out["algorithmic_bytes_per_layer"] = float(np.mean(bytes_))
+            assert TS.device_error() == 0
+            res[f"{name}_T{T}"] = out
+        del st
+    return res
+
+
 def bench_staged(args):
     """Host-staged experts: one Qwen-shaped decode layer (256 IQ3_XXS experts) whose experts all sit in pinned host
     memory, 64 of them in HBM slots; T tokens a step.  The layer-by-layer step (router, top-8, staged grouping with the
@@ -658,14 +731,22 @@ def main():
     ap.add_argument("--layers", type=int, default=40, help="profiling captures only: fewer resident layers")
     ap.add_argument("--trace", action="store_true", help="print the fused kernel's per-phase timeline (stderr)")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen", "staged"],
+                    choices=["decode", "prefill", "prefill_lfm", "ep", "ep_qwen", "staged", "decode_act"],
                     help="decode: the headline C1 line; prefill: the C2 Gemma-shaped prefill layer (--tokens 8192); "
                          "prefill_lfm: the C3 LFM2-shaped layer (--tokens 2048); ep: the C2 layer expert-parallel "
                          "over the launched ranks; ep_qwen: the C4 Qwen IQ3 layer expert-parallel (65536 tokens); "
-                         "staged: a decode layer with its experts in host memory, 64 of 256 in HBM slots")
+                         "staged: a decode layer with its experts in host memory, 64 of 256 in HBM slots; "
+                         "decode_act: the Gemma 4 / LFM2 decode layer, layer by layer and in one launch")
     args = ap.parse_args()
     if args.workload == "staged":
         return bench_staged(args)
+    if args.workload == "decode_act":
+        import torch
+        torch.cuda.set_device(0)
+        with Clocks(0) as clk:
+            r = act_decode_measure(torch.device("cuda", 0), args.steps, args.warmup)
+        print(json.dumps({"workload": "gemma / lfm decode layer", **r, "clocks": clk.summary()}), flush=True)
+        return 0
     if args.workload == "ep_qwen":
         return bench_ep_qwen(args)
     if args.workload in ("prefill", "prefill_lfm", "ep"):
@@ -870,6 +951,7 @@ def bench_decode(args):
                 extras[key] = {k: r[k] for k in ("metric", "value", "unit", "us_per_layer", "ms_per_step", "dtype",
                                                  "config", "roofline", "e2e", "clocks", "cpu_baseline")}
                 extras[key]["gpu_launches"] = r["gpu_launches_per_step"] * 10
+            extras["gemma_lfm_decode"] = act_decode_measure(device)
         r = ep_qwen_measure(args, 5, 3, own_group=(ws == 1))
         if r is not None:
             extras["ep_c4"] = {k: r[k] for k in ("metric", "value", "unit", "n_gpus", "us_per_layer", "ms_per_step",

@@ -252,6 +252,37 @@ int tsb_moe_decode_set_trace(unsigned long long* buf);
  * Process-wide.  No counterpart in the reference. */
 int tsb_moe_decode_set_debug(int withhold_cta);
 
+/* ---- the Gemma 4 / LFM2 decode MoE block in one launch.  Replaces the per-layer decode sequence of those engines
+ * (src/gemma4/engine.cpp:2436-2457: route_rows, gemma_native_mmvq_ids gate/up, geglu_rows / swiglu_clamp_rows, the
+ * hidden rows' q8_1, gemma_native_mmvq_ids down, moe_sum; and the dense shared MLP's gate/up, activation, q8_1 and
+ * down).  Per token t: logits = router . h[t] (router fp32 [n_expert][n_embd]); picks and weights as tsb_route_rows
+ * (gate, in_scale, bias, escale, norm, w_scale); out[t] (+)= sum_k w[t,k] down_k(q8_1(act(gate_k . hq[t], up_k .
+ * hq[t]))) in pick order, as tsb_moe_sum; with a shared MLP (sh_n_ff > 0, blob in the expert layout of the same
+ * formats) sh_out[t] = its output (sh_act).  Every value equals the layer-by-layer entry points' bit for bit.  The
+ * workspace begins with the router logits [n_tok][n_expert].  Weights Q4_0 / Q4_0 or Q4_K / Q6_K (gate-up / down);
+ * 1..16 tokens, n_tok * n_used <= 128, n_expert a multiple of 32 up to 512, rows of up to 256 calls. */
+typedef struct tsb_decode_act_desc {
+    uint32_t struct_size;   /* sizeof(tsb_decode_act_desc) */
+    int32_t n_tok, n_embd, n_ff, n_expert, n_used, sh_n_ff;
+    int32_t gu_type, d_type;
+    int32_t act, sh_act;    /* 0 SwiGLU, 1 GELU-tanh, 2 clamped SwiGLU (limit) */
+    float limit;
+    int32_t gate;           /* 0 softmax of logit * in_scale, 1 sigmoid */
+    float in_scale;
+    int32_t norm;
+    float w_scale;
+} tsb_decode_act_desc;
+uint64_t tsb_moe_decode_act_workspace_bytes(const tsb_decode_act_desc* d);
+/* Phase stamps of tsb_moe_decode_act: with a device buffer of (SM count) * 8 u64, every CTA stores the global timer
+ * at its start, end of phase A, after barrier 1, after routing, end of phase B, after barrier 2, after quantising the
+ * hidden rows and at its end; null turns it off.  Process-wide; a captured graph keeps the buffer it was captured
+ * with.  No counterpart in the reference. */
+int tsb_moe_decode_act_set_trace(unsigned long long* buf);
+int tsb_moe_decode_act(const tsb_decode_act_desc* d, const float* router, const float* bias, const float* escale,
+                       const float* h, const void* hq, const void* blobs, uint64_t blob_stride, const void* sh_blob,
+                       float* out, int accumulate, float* sh_out, int32_t* ids, float* w, void* workspace,
+                       uint64_t ws_bytes, void* stream);
+
 /* --------------------------------------------------------------------------------------------- small products */
 /* Up to TSB_MMVQ_MAX matrices of one ggml type and shape [n_out][n_in] in one launch, each times its own q8_1 column
  * (n_in / 32 blocks): y[i][r] = row r of w[i] . x[i], each value the reference's iq_mmvq row dot bit for bit (the

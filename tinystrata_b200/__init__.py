@@ -52,6 +52,14 @@ class DecodeDesc(C.Structure):
                 ("eps", C.c_float)]
 
 
+class DecodeActDesc(C.Structure):
+    """tsb_decode_act_desc: the Gemma 4 / LFM2 decode MoE block of one launch."""
+    _fields_ = [("struct_size", C.c_uint32), ("n_tok", C.c_int32), ("n_embd", C.c_int32), ("n_ff", C.c_int32),
+                ("n_expert", C.c_int32), ("n_used", C.c_int32), ("sh_n_ff", C.c_int32), ("gu_type", C.c_int32),
+                ("d_type", C.c_int32), ("act", C.c_int32), ("sh_act", C.c_int32), ("limit", C.c_float),
+                ("gate", C.c_int32), ("in_scale", C.c_float), ("norm", C.c_int32), ("w_scale", C.c_float)]
+
+
 class ExpertLayout(C.Structure):
     """tsb_expert_layout (the reference's NativeExpertLayout, iq_kernels.hpp:45-53)."""
     _fields_ = [("gu_type", C.c_int32), ("d_type", C.c_int32), ("n_embd", C.c_int64), ("n_ff", C.c_int64),
@@ -130,6 +138,10 @@ SIGNATURES = {
     "tsb_ep_destroy": (C.c_int, [_p]),
     "tsb_moe_layer_tail": (C.c_int, [_p, _p, _p, _p, _p, _f, C.c_int, C.c_int, _f, _p]),
     "tsb_set_wait_limit_ns": (C.c_int, [_u64]),
+    "tsb_moe_decode_act_workspace_bytes": (_u64, [C.POINTER(DecodeActDesc)]),
+    "tsb_moe_decode_act_set_trace": (C.c_int, [_p]),
+    "tsb_moe_decode_act": (C.c_int, [C.POINTER(DecodeActDesc), _p, _p, _p, _p, _p, _p, _u64, _p, _p, C.c_int, _p, _p,
+                                     _p, _p, _u64, _p]),
     "tsb_moe_group_staged": (C.c_int, [_p, C.c_int, C.c_int, C.c_int, _p, C.c_int, _p, _p, _u64, _p, C.c_int, _p, _p,
                                        _p, _p, _p, _p, _p]),
     "tsb_staged_rebalance": (C.c_int, [_p, C.c_int, C.c_int, _p, _p, C.c_int, _p, _p]),
@@ -265,6 +277,34 @@ def moe_group(ids, n_expert: int, blobs, blob_stride: int, groups: Groups | None
                                _ptr(groups.grp_start), _ptr(groups.n_groups), _ptr(groups.ent_dst),
                                _ptr(groups.ent_tok), _stream(stream)), "moe_group")
     return groups
+
+
+def decode_act_desc(cfg: dict, n_tok: int, shared: bool) -> DecodeActDesc:
+    """The descriptor of a Gemma / LFM layer config (router_mode softmax_scaled: gate 0; sigmoid: gate 1)."""
+    d = DecodeActDesc()
+    d.struct_size = C.sizeof(DecodeActDesc)
+    d.n_tok, d.n_embd, d.n_ff = n_tok, cfg["n_embd"], cfg["n_ff"]
+    d.n_expert, d.n_used = cfg["n_expert"], cfg["n_used"]
+    d.sh_n_ff = (cfg.get("sh_n_ff") or 0) if shared else 0
+    d.gu_type, d.d_type = cfg["gu_type"], cfg["d_type"]
+    d.act, d.sh_act = cfg["act"], cfg.get("sh_act", cfg["act"])
+    d.limit = cfg.get("limit", float("inf"))
+    sig = cfg["router_mode"] == "sigmoid"
+    d.gate = 1 if sig else 0
+    d.in_scale = 1.0 if sig else cfg.get("in_scale", 1.0)
+    d.norm = 1
+    d.w_scale = cfg.get("w_scale", 0.0) if sig else 0.0
+    return d
+
+
+def moe_decode_act(desc: DecodeActDesc, router, h, hq, blobs, blob_stride: int, out, ws, bias=None, escale=None,
+                   sh_blob=None, sh_out=None, ids=None, w=None, accumulate: bool = True, stream=None):
+    """The Gemma / LFM decode MoE block in one launch (tsb_moe_decode_act)."""
+    _check(lib().tsb_moe_decode_act(C.byref(desc), _ptr(router), _ptr(bias), _ptr(escale), _ptr(h), _ptr(hq),
+                                    _ptr(blobs), blob_stride, _ptr(sh_blob), _ptr(out), int(accumulate), _ptr(sh_out),
+                                    _ptr(ids), _ptr(w), _ptr(ws), ws.numel() * ws.element_size(), _stream(stream)),
+           "moe_decode_act")
+    return out
 
 
 def moe_group_staged(ids, n_expert: int, slot_of, n_slots: int, slots, host_blobs, blob_stride: int, stage,

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtsb_moe.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["tsb_moe.cu", "tsb_decode.cu", "tsb_ep.cu", "tsb_staged.cu", "tsb_gguf.cpp"]
+SOURCES = ["tsb_moe.cu", "tsb_decode.cu", "tsb_decode_act.cu", "tsb_ep.cu", "tsb_staged.cu", "tsb_gguf.cpp"]
 # every header of the sources: a change to any of them rebuilds both objects
 HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith((".cuh", ".inc"))) + ["../../include/tsb_moe.h"]
 FLAGS = ["-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-Xcompiler", "-fPIC",

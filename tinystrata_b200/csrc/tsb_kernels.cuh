@@ -131,6 +131,73 @@ __device__ __forceinline__ float act_value(int act, float g, float u, float limi
     return __fmul_rn(fdiv_fm(g, 1.0f + __expf(-g)), u);
 }
 
+// ------------------------------------------------------------------------------------------------ Gemma / LFM routing
+// One token's routing by one warp (route_kernel, gemma4/kernels.cu:289-356; built without fast-math, as that file):
+// gate 0 softmax of logit * in_scale, gate 1 sigmoid; pick on p + bias (lowest id on ties); w = p [/ max(sum, floor)]
+// [* escale] [* w_scale].  lgf(e) gives logit e; PER experts a lane; lanes < n_used write ids_out / w_out.
+template <int PER, class LG>
+__device__ __forceinline__ void route_row_warp(const LG& lgf, int n_expert, int n_used, int gate, float in_scale,
+                                               const float* __restrict__ bias, const float* __restrict__ escale,
+                                               int norm, float w_scale, int lane, int32_t* ids_out, float* w_out) {
+    float p[PER], pick[PER];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int e = lane + k * 32;
+        p[k] = e < n_expert ? lgf(e) * in_scale : -INFINITY;
+        mx = fmaxf(mx, p[k]);
+    }
+    if (gate == 0) {
+        mx = warp_max(mx);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            p[k] = lane + k * 32 < n_expert ? expf(p[k] - mx) : 0.0f;
+            sum += p[k];
+        }
+        const float inv = __fdiv_rn(1.0f, warp_sum(sum));
+#pragma unroll
+        for (int k = 0; k < PER; ++k) p[k] *= inv;
+    } else {
+#pragma unroll
+        for (int k = 0; k < PER; ++k) p[k] = __fdiv_rn(1.0f, 1.0f + expf(-p[k]));
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int e = lane + k * 32;
+        pick[k] = e < n_expert ? p[k] + (bias ? bias[e] : 0.0f) : -INFINITY;
+    }
+    float sum = 0.0f, mine = 0.0f;
+    int my_id = 0;
+    for (int j = 0; j < n_used; ++j) {
+        float best = -INFINITY;
+        int at = n_expert;
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (pick[k] > best) best = pick[k], at = lane + k * 32;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float b = __shfl_xor_sync(0xffffffffu, best, o);
+            const int a = __shfl_xor_sync(0xffffffffu, at, o);
+            if (b > best || (b == best && a < at)) best = b, at = a;
+        }
+        float pw = 0.0f;
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+            if (lane + k * 32 == at) pw = p[k], pick[k] = -INFINITY;
+        pw = __shfl_sync(0xffffffffu, pw, at % 32);
+        sum += pw;
+        if (lane == j) mine = pw, my_id = at;
+    }
+    if (lane >= n_used) return;
+    float v = mine;
+    if (norm) v = __fdiv_rn(v, fmaxf(sum, 6.103515625e-5f));
+    if (escale) v *= escale[my_id];
+    if (w_scale != 0.0f) v *= w_scale;
+    ids_out[lane] = my_id;
+    w_out[lane] = v;
+}
+
 // ------------------------------------------------------------------------------------------------ row dots
 // One warp, one row staged at `row` (shared memory): lane calls k = lane + 32 j (j < J) for C calls per row; the NC
 // activations' per-lane partial sums in s[], then the xor tree.  The per-lane order and the tree are row_dot's

@@ -19,6 +19,7 @@
 namespace tsb {
 
 int decode_set_wait_limit(unsigned long long ns);   // tsb_decode.cu: that translation unit's copy of the bound
+int decode_act_set_wait_limit(unsigned long long ns);   // tsb_decode_act.cu: its copy of the bound
 
 // ================================================================================================ host error state
 static thread_local char g_err[512] = "";
@@ -73,6 +74,13 @@ static DevInfo* dev_info() {
     }
     return &I;
 }
+
+// The current device's error word, for the entry points of the other translation units.
+unsigned* device_error_word() {
+    DevInfo* di = dev_info();
+    return di ? di->err : nullptr;
+}
+
 // Opt kernel `bit` of this device into `bytes` of dynamic shared memory once (the attribute is per device).
 template <typename K>
 static int smem_optin(DevInfo* di, int bit, K kern, size_t bytes, const char* what) {
@@ -223,9 +231,8 @@ __global__ void __launch_bounds__(256) k_route_topk(const float* __restrict__ lo
     if (lane < K) weights[lane] = selected * inv;
 }
 
-// Gemma / LFM routing (route_kernel, gemma4/kernels.cu:289-356; that file is built without fast-math): gate 0 softmax
-// of logit * in_scale, gate 1 sigmoid; pick on p + bias (lowest id on ties); w = p [/ max(sum, floor)] [* escale]
-// [* w_scale].  A warp per token, PER experts a lane.
+// Gemma / LFM routing (route_kernel, gemma4/kernels.cu:289-356; that file is built without fast-math): a warp per
+// token, PER experts a lane (route_row_warp, tsb_kernels.cuh).
 template <int PER>
 __global__ void __launch_bounds__(256) k_route_rows(const float* __restrict__ logits, int n_expert, int n_used, int rows,
                                                     int gate, float in_scale, const float* __restrict__ bias,
@@ -234,63 +241,8 @@ __global__ void __launch_bounds__(256) k_route_rows(const float* __restrict__ lo
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const float* lg = logits + (size_t) row * n_expert;
-    float p[PER], pick[PER];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int e = lane + k * 32;
-        p[k] = e < n_expert ? lg[e] * in_scale : -INFINITY;
-        mx = fmaxf(mx, p[k]);
-    }
-    if (gate == 0) {
-        mx = warp_max(mx);
-        float sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < PER; ++k) {
-            p[k] = lane + k * 32 < n_expert ? expf(p[k] - mx) : 0.0f;
-            sum += p[k];
-        }
-        const float inv = __fdiv_rn(1.0f, warp_sum(sum));
-#pragma unroll
-        for (int k = 0; k < PER; ++k) p[k] *= inv;
-    } else {
-#pragma unroll
-        for (int k = 0; k < PER; ++k) p[k] = __fdiv_rn(1.0f, 1.0f + expf(-p[k]));
-    }
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int e = lane + k * 32;
-        pick[k] = e < n_expert ? p[k] + (bias ? bias[e] : 0.0f) : -INFINITY;
-    }
-    float sum = 0.0f, mine = 0.0f;
-    int my_id = 0;
-    for (int j = 0; j < n_used; ++j) {
-        float best = -INFINITY;
-        int at = n_expert;
-#pragma unroll
-        for (int k = 0; k < PER; ++k)
-            if (pick[k] > best) best = pick[k], at = lane + k * 32;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float b = __shfl_xor_sync(0xffffffffu, best, o);
-            const int a = __shfl_xor_sync(0xffffffffu, at, o);
-            if (b > best || (b == best && a < at)) best = b, at = a;
-        }
-        float pw = 0.0f;
-#pragma unroll
-        for (int k = 0; k < PER; ++k)
-            if (lane + k * 32 == at) pw = p[k], pick[k] = -INFINITY;
-        pw = __shfl_sync(0xffffffffu, pw, at % 32);
-        sum += pw;
-        if (lane == j) mine = pw, my_id = at;
-    }
-    if (lane >= n_used) return;
-    float v = mine;
-    if (norm) v = __fdiv_rn(v, fmaxf(sum, 6.103515625e-5f));
-    if (escale) v *= escale[my_id];
-    if (w_scale != 0.0f) v *= w_scale;
-    ids[(size_t) row * n_used + lane] = my_id;
-    w[(size_t) row * n_used + lane] = v;
+    route_row_warp<PER>([&](int e) { return lg[e]; }, n_expert, n_used, gate, in_scale, bias, escale, norm, w_scale,
+                        lane, ids + (size_t) row * n_used, w + (size_t) row * n_used);
 }
 
 // Decode grouping (k_group, q36_engine.cu:396-422): groups of ascending expert id, entries in entry order.  One CTA;
@@ -666,6 +618,7 @@ int tsb_set_wait_limit_ns(uint64_t ns) {
     const unsigned long long v = ns;
     if (cudaMemcpyToSymbol(g_wait_ns, &v, sizeof v) != cudaSuccess) return cuda_status("set_wait_limit_ns");
     if (decode_set_wait_limit(v) != TSB_OK) return cuda_status("set_wait_limit_ns (decode)");
+    if (decode_act_set_wait_limit(v) != TSB_OK) return cuda_status("set_wait_limit_ns (decode_act)");
     return TSB_OK;
 }
 

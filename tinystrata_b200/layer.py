@@ -11,9 +11,9 @@ import torch
 
 import numpy as np
 
-from . import (ACT_SWIGLU, Groups, Q8_1_BYTES, moe_combine, moe_group, moe_group_staged, moe_sum,
-               native_expert_grouped, native_expert_layout, native_expert_scratch_bytes, native_router_topk,
-               route_rows, router_logits_f32, staged_load, staged_rebalance)
+from . import (ACT_SWIGLU, Groups, Q8_1_BYTES, decode_act_desc, lib, moe_combine, moe_decode_act, moe_group,
+               moe_group_staged, moe_sum, native_expert_grouped, native_expert_layout, native_expert_scratch_bytes,
+               native_router_topk, route_rows, router_logits_f32, staged_load, staged_rebalance)
 
 
 class StagedExperts:
@@ -107,6 +107,30 @@ class MoELayer:
             self.sh_groups.ent_tok.copy_(torch.arange(max_tokens, dtype=torch.int32))
             self.sh_groups.n_groups.fill_(1)
             self._sh_T = -1
+
+    def forward_fused(self, x: torch.Tensor, h: torch.Tensor, hq: torch.Tensor, stream=None):
+        """Gemma / LFM decode (router_mode softmax_scaled or sigmoid) in one launch (tsb_moe_decode_act): the same
+        values as forward bit for bit -- x += the picks' weighted sum (+ the shared MLP's output); ids, w, shared and
+        the logits (self.fused_logits) as forward leaves them."""
+        import ctypes as C
+        cfg = self.cfg
+        assert cfg["router_mode"] in ("softmax_scaled", "sigmoid") and self.staged is None
+        T = x.shape[0]
+        shared = self.Ls is not None
+        if getattr(self, "_act_ws", None) is None:
+            big = decode_act_desc(cfg, self.max_tokens, shared)
+            n = int(lib().tsb_moe_decode_act_workspace_bytes(C.byref(big)))
+            self._act_ws = torch.empty(n // 4 + 64, dtype=torch.float32, device=self.dev)
+        d = decode_act_desc(cfg, T, shared)
+        sig = cfg["router_mode"] == "sigmoid"
+        moe_decode_act(d, self.router, h, hq, self.blobs, self.stride, x, self._act_ws,
+                       bias=self.bias if sig else None, escale=None if sig else self.escale,
+                       sh_blob=self.sh_blob if shared else None, sh_out=self.shared[:T] if shared else None,
+                       ids=self.ids[:T], w=self.w[:T], accumulate=True, stream=stream)
+        self.fused_logits = self._act_ws[:T * self.E].view(T, self.E)
+        if shared:
+            x.add_(self.shared[:T])
+        return x
 
     def _shared_for(self, T: int):
         if self._sh_T != T:
