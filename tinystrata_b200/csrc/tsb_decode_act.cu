@@ -726,13 +726,13 @@ int tsb_moe_decode_act(const tsb_decode_act_desc* d, const float* router, const 
         (FS > 0 && ((uintptr_t) sh_blob % 16 || sh_bytes % 16)))
         return afail(TSB_ERR_ALIGN, "decode_act: blobs, stride, gate/up rows and blob sizes must be 16-byte multiples");
     // rows per unit (gate/up, down) and staging depth: one gate/up row pair and two down rows per unit, four buffers
-    // deep, measured fastest wherever a step uses few experts; from 32 entries (about 30 distinct experts) the down
-    // units take 8 rows of each expert, so that a warp's share of every used expert's rows comes in fewer, larger
-    // pieces.  The deepest staging that fits beside the hidden rows (two at least).
+    // deep, measured fastest wherever a step uses few experts; from 32 entries (about 30 distinct experts) units of two
+    // gate/up row pairs and 8 down rows of each expert, so that a warp's share comes in fewer, larger pieces.  The
+    // first choice whose staging fits beside the hidden rows two deep at least, as deep as fits up to four.
     static const int kFew[1][2] = {{1, 2}};
-    static const int kMany[3][2] = {{1, 8}, {1, 4}, {1, 2}};
+    static const int kMany[4][2] = {{2, 8}, {2, 4}, {1, 4}, {1, 2}};
     const int (*choice)[2] = T * K >= 32 ? kMany : kFew;
-    const int n_choice = T * K >= 32 ? 3 : 1;
+    const int n_choice = T * K >= 32 ? 4 : 1;
     int br = 0, ar = 0, nst = 0;
     uint64_t sb = 0;
     for (int i = 0; i < n_choice && !nst; ++i) {
