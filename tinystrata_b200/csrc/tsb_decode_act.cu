@@ -3,14 +3,14 @@
 // The reference runs the decode MoE block of these engines as a chain of launches (src/gemma4/engine.cpp:2436-2457:
 // route_rows, the experts' gate/up gemma_native_mmvq_ids, geglu_rows / swiglu_clamp_rows, the hidden rows' q8_1,
 // the down gemma_native_mmvq_ids, moe_sum; the dense shared MLP beside it).  Here one persistent CTA per SM runs the
-// whole block in three phases, separated by two grid barriers (bounded waits):
+// whole block in three phases, separated by grid barriers (bounded waits):
 //   A  the router logits (the fp32 GEMV, one warp per expert row) and the shared MLP's gate/up rows -> its hidden
 //      vectors;
 //   B  every CTA routes every token itself (the route_kernel arithmetic) and groups the entries by expert (k_group's
 //      order); the routed experts' gate/up rows -> hidden vectors;
-//   C  every CTA quantises all hidden vectors (routed and shared) to q8_1 in shared memory; a warp takes rows of the
-//      down matrices of every used expert and sums its picks' weighted rows in pick order (moe_sum) straight into the
-//      output, or rows of the shared MLP's down matrix.
+//   C  the hidden vectors (routed and shared) are quantised to q8_1 once over the grid (a third barrier) and copied
+//      into every CTA's shared memory; a warp takes rows of the down matrices of every used expert and sums its picks'
+//      weighted rows in pick order (moe_sum) straight into the output, or rows of the shared MLP's down matrix.
 // Weight rows are read in place from HBM by the warps (no staging): each lane's calls of a row are independent loads.
 // Every value is computed by the same device code as the layer-by-layer kernels (row_dot's per-lane order and xor
 // tree, act_value, the q8_1 quantiser, route_row_warp, the router GEMV's expression, moe_sum's order), so the outputs
@@ -36,7 +36,6 @@ constexpr int kAWarps = 8;
 constexpr int kAThreads = kAWarps * 32;
 constexpr int kAJ = 8;           // calls per lane: rows of up to 256 calls
 constexpr int kAJQ4K = 4;        // Q4_K gate/up rows: up to 128 calls (n_embd <= 2048), fewer registers
-constexpr int kARMax = 8;        // routed down rows per unit (of every used expert): 2, 4 or 8, chosen by the host
 constexpr int kASR = 2;          // shared down rows per unit
 constexpr int kAMaxT = 16;
 constexpr int kAMaxEnt = 128;
@@ -73,6 +72,7 @@ struct ActParams {
     float* logits;                // workspace [T][E]
     float* hid;                   // workspace [T * K][F]
     float* shid;                  // workspace [T][FS]
+    BlockQ8_1* hqh;               // workspace: q8_1 of the routed hidden rows, then of the shared MLP's
     unsigned* bar;                // workspace: arrival count, generation (zero before the launch)
     unsigned* err;
     unsigned long long blob_bytes, sh_bytes;
@@ -157,31 +157,6 @@ __device__ __forceinline__ QB qb_from_smem(const BlockQ8_1* b) {
     r.d = __low2float(b->ds);
     return r;
 }
-// n fp32 rows of F values (written by other CTAs of this launch: L2 loads) -> q8_1 blocks in shared memory, a block a
-// thread (q8_1_lane: the same bits as the warp quantiser).
-__device__ void quantize_rows_smem(const float* src, int rows, int F, BlockQ8_1* dst) {
-    const int nb = rows * (F / 32);
-    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-        const int r = b / (F / 32), c = b % (F / 32);
-        const float4* p4 = (const float4*) (src + (size_t) r * F + 32 * c);
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 f = __ldcg(p4 + i);
-            v[4 * i] = f.x;
-            v[4 * i + 1] = f.y;
-            v[4 * i + 2] = f.z;
-            v[4 * i + 3] = f.w;
-        }
-        const Q8Block q = q8_1_lane(v);
-        BlockQ8_1* o = dst + b;
-        o->ds = q.ds;
-        int* ow = (int*) o->qs;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ow[i] = q.q[i];
-    }
-}
-
 template <int PER>
 __device__ __forceinline__ void route_token(const ActParams& p, int t, int lane, int32_t* ids_s, float* w_s) {
     const float* lg = p.logits + (size_t) t * p.E;
@@ -190,7 +165,8 @@ __device__ __forceinline__ void route_token(const ActParams& p, int t, int lane,
 }
 
 // Phase stamps (globaltimer) of every CTA when a trace buffer is set: [CTA][8] = start, phase A done, barrier 1
-// passed, routed and grouped, phase B done, barrier 2 passed, hidden rows quantised, end.
+// passed, routed and grouped, phase B done, barrier 2 passed, hidden rows quantised (over the grid, barrier 3) and in
+// shared memory, end.
 __device__ unsigned long long* g_act_trace = nullptr;
 __device__ __forceinline__ void act_stamp(int ev) {
     unsigned long long* t = g_act_trace;
@@ -304,7 +280,9 @@ __global__ void __launch_bounds__(kAThreads, 1) k_decode_act(ActParams p) {
     }
 
     // ---------------------------------------------------------------- A: router logits, shared gate/up
-    for (long long u = gw; u < p.E; u += W) {   // router row u (fp32, direct loads): k_router_logits' expression and order
+    // phase A deals its units by pw = warp * grid + CTA, so that the router rows land on different CTAs
+    const long long pw = (long long) warp * gridDim.x + blockIdx.x;
+    for (long long u = pw; u < p.E; u += W) {   // router row u (fp32, direct loads): k_router_logits' expression and order
         const int o = (int) u;
         const float4* wr = (const float4*) (p.router + (size_t) o * H);
         float acc[kAMaxT];
@@ -328,7 +306,7 @@ __global__ void __launch_bounds__(kAThreads, 1) k_decode_act(ActParams p) {
             }
     }
     if (p.sh) {   // shared gate/up rows: warp w takes rows w, w + W, ... after the router rows of the same sequence
-        const int first = (int) (gw < p.E ? gw + ((p.E - gw + W - 1) / W) * W : gw);
+        const int first = (int) (pw < p.E ? pw + ((p.E - pw + W - 1) / W) * W : pw);
         const int nA = p.E + p.FS, Wi = (int) W;
         const int n = first < nA ? (nA - first + Wi - 1) / Wi : 0;
         if (T <= NC) load_in(0, T);
@@ -470,9 +448,28 @@ __global__ void __launch_bounds__(kAThreads, 1) k_decode_act(ActParams p) {
 
     // ---------------------------------------------------------------- C: routed down rows + pick-order sum; shared down
     BlockQ8_1* q8s = q8 + (size_t) n_ent * (F / 32);   // the shared hidden rows after the routed ones
-    quantize_rows_smem(p.hid, n_ent, F, q8);
-    if (p.sh) quantize_rows_smem(p.shid, T, p.FS, q8s);
-    __syncthreads();
+    {
+        // every hidden row's q8_1 once over the grid (a warp per block: q8_1_warp, the same bits as the layer-by-layer
+        // kernels' q8_1_lane), then into every CTA's shared memory
+        const int nbr = n_ent * (F / 32), nbt = nbr + (p.sh ? T * (p.FS / 32) : 0);
+        for (long long b = gw; b < nbt; b += W) {
+            const float* src = b < nbr ? p.hid + (size_t) (b / (F / 32)) * F + 32 * (b % (F / 32))
+                                       : p.shid + (size_t) ((b - nbr) / (p.FS / 32)) * p.FS + 32 * ((b - nbr) % (p.FS / 32));
+            float d, sum;
+            const int8_t q = q8_1_warp(__ldcg(src + lane), d, sum);
+            p.hqh[b].qs[lane] = q;
+            if (lane == 0) p.hqh[b].ds = make_half2(__float2half(q8_finite(d)), __float2half(q8_finite(sum)));
+        }
+        __syncthreads();
+        grid_barrier(p.bar, p.err, 0x612u);
+        const uint32_t bytes = ((uint32_t) nbt * (uint32_t) sizeof(BlockQ8_1) + 15u) & ~15u;
+        const uint32_t dst = smem_u32(q8);
+        for (uint32_t o = threadIdx.x * 16u; o < bytes; o += blockDim.x * 16u)
+            cp_async16(dst + o, (const uint8_t*) p.hqh + o);
+        cp_commit();
+        cp_wait_all();
+        __syncthreads();
+    }
     act_stamp(6);
     {
         // routed units u < nR: AR rows of every used expert's down matrix, one item per group (gi items), summed per
@@ -614,7 +611,7 @@ int launch_act(const ActParams& p, size_t smem, int sms, int dev, int which, cud
 }
 
 struct ActWs {
-    size_t logits, hid, shid, bar, total;
+    size_t logits, hid, shid, hqh, bar, total;
 };
 ActWs act_ws(const tsb_decode_act_desc* d) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t) 255; };
@@ -623,6 +620,8 @@ ActWs act_ws(const tsb_decode_act_desc* d) {
     w.logits = o; o += al((size_t) d->n_tok * d->n_expert * 4);
     w.hid = o;    o += al((size_t) d->n_tok * d->n_used * d->n_ff * 4);
     w.shid = o;   o += al((size_t) d->n_tok * (d->sh_n_ff > 0 ? d->sh_n_ff : 1) * 4);
+    w.hqh = o;    o += al(((size_t) d->n_tok * d->n_used * (d->n_ff / 32) +
+                           (size_t) d->n_tok * (d->sh_n_ff > 0 ? d->sh_n_ff / 32 : 0)) * sizeof(BlockQ8_1));
     w.bar = o;    o += 256;
     w.total = o;
     return w;
@@ -772,6 +771,7 @@ int tsb_moe_decode_act(const tsb_decode_act_desc* d, const float* router, const 
     p.logits = (float*) (ws + wl.logits);
     p.hid = (float*) (ws + wl.hid);
     p.shid = (float*) (ws + wl.shid);
+    p.hqh = (BlockQ8_1*) (ws + wl.hqh);
     p.bar = (unsigned*) (ws + wl.bar);
     p.err = device_error_word();
     if (!p.err) return afail(TSB_ERR_CUDA, "decode_act: device error word");
