@@ -9,7 +9,8 @@ each rank runs its own replica (weak scaling) and `value` sums the replicas.
 
 The same line carries the other configurations as keys: decode_sweep (T = 2, 4, 16), prefill_c2 (Gemma-4-shaped Q4_0
 layer, T = 8192) and prefill_c3 (LFM2.5-shaped Q4_K / Q6_K layer, T = 2048) on one GPU, each with its CPU baseline
-where one exists, gemma_lfm_decode (the Gemma 4 / LFM2 decode layer, layer by layer and in one launch), and ep_c4 (the Qwen IQ3 layer over T = 65536 tokens, experts sharded over every rank of the run).
+where one exists, gemma_lfm_decode (the Gemma 4 / LFM2 decode layer, layer by layer and in one launch), and ep_c4
+(the Qwen IQ3 layer over T = 65536 tokens, experts sharded over every rank of the run).
 --workload selects one of them alone.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl tsb|reference]
